@@ -1,0 +1,414 @@
+#!/usr/bin/env python
+"""MoE-block benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: the Mixtral-shaped block (T=4096 tokens per GPU, H=4096, I=14336,
+E=8, top-2, bf16 experts, fp32 router), synthetic inputs drawn from seeded
+generators.  A step is one forward of the block over one batch: router,
+dispatch, gate/up GEMM with fused SwiGLU, down GEMM, combine.
+
+  value      whole-job tokens/s with inputs resident in HBM: K replays of a
+             CUDA graph of one step, CUDA events on the launching stream,
+             barrier + synchronize on both sides, max over ranks.
+  e2e        the same metric through MoEBlock.__call__ with the step's x copied
+             from pinned host memory and the output copied back, every step.
+  roofline   the gate/up+SwiGLU GEMM (the dominant kernel): algorithmic FLOPs
+             per launch / its mean CUDA-event duration over K eager steps.
+  cpu_baseline  the CPU oracle (a C restatement of the reference's path) on a
+             bounded token sample of the same workload, rank 0, N=1 only.
+
+With N > 1 (torchrun, one process per GPU) each rank runs the block on its
+own T tokens with its own weights (independent replicas, weak scaling).
+`--impl reference` times the CPU port of the reference's path instead (rank 0
+only; the other ranks exit without work).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "cuda-moe-engine_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "MoE-block tokens/s/GPU (H4096 I14336 E8 top2); dispatch+combine HBM GB/s"
+KERNELS_PER_STEP = 7  # route: logits + top-k; dispatch: index + pack; 2 GEMMs; combine
+
+
+def parse_args():
+    parser = argparse.ArgumentParser(description="MoE block benchmark")
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    parser.add_argument("--workload", default="mixtral")
+    parser.add_argument("--cpu-sample-tokens", type=int, default=64)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    return parser.parse_args()
+
+
+def dist_info():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi samples (200 ms) of SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=10)
+
+    def summary(self):
+        self.file.flush()
+        rows = [line.split(",") for line in Path(self.file.name).read_text().splitlines()]
+        rows = [[c.strip() for c in r] for r in rows if len(r) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, value in zip(names, r[5:9]):
+                if value.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], data.get("bf16_tflops_sustained"), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profiled_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary, if any."""
+    for path in sorted((ROOT / "profiles").glob("*.md")):
+        match = re.search(rf"{kernel}\s+traffic_bytes_per_launch:\s*([0-9.eE+]+)", path.read_text())
+        if match:
+            return float(match.group(1))
+    return None
+
+
+# ----------------------------------------------------------- our GPU path
+def build_block(workload, device, seed_offset=0):
+    """Mixtral-shaped block with weights drawn on the GPU (per-expert generators)."""
+    from moe_dispatch.layer import MoEBlock, MoEConfig, MoEWeights
+
+    w = workload
+    cfg = MoEConfig(w.hidden, w.intermediate, w.experts, w.topk)
+    g = torch.Generator(device=device).manual_seed(1000 + w.seed + seed_offset)
+    router = torch.randn(w.experts, w.hidden, device=device, generator=g) / w.hidden**0.5
+    gate_up = torch.empty(w.experts, 2 * w.intermediate, w.hidden, device=device, dtype=torch.bfloat16)
+    down = torch.empty(w.experts, w.hidden, w.intermediate, device=device, dtype=torch.bfloat16)
+    for e in range(w.experts):
+        gate_up[e] = (torch.randn(2 * w.intermediate, w.hidden, device=device, generator=g)
+                      / w.hidden**0.5).to(torch.bfloat16)
+        down[e] = (torch.randn(w.hidden, w.intermediate, device=device, generator=g)
+                   / w.intermediate**0.5).to(torch.bfloat16)
+    block = MoEBlock(cfg, device=device, weights=MoEWeights(router, gate_up, down))
+    x = torch.randn(w.tokens, w.hidden, device=device, generator=g).to(torch.bfloat16)
+    return block, x
+
+
+def step_instrumented(block, x, events):
+    """One forward with events around the gate/up GEMM and the transport kernels."""
+    state = block.workspace(x)
+    transport = state.transport
+    ext = block.extension
+    ids32, ids64, weights = block.route(x)
+    events["dispatch"][0].record()
+    transport.dispatch(x, ids32, ids64)
+    events["dispatch"][1].record()
+    events["gemm1"][0].record()
+    ext.grouped_gemm_swiglu_out(transport.packed, block.gate_up_weight, transport.offsets,
+                                state.activated)
+    events["gemm1"][1].record()
+    events["gemm2"][0].record()
+    ext.grouped_gemm_out(state.activated, block.down_weight, transport.offsets,
+                         state.expert_output)
+    events["gemm2"][1].record()
+    events["combine"][0].record()
+    transport.combine(state.expert_output, weights)
+    events["combine"][1].record()
+    return transport.output
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(value, world, device):
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_ours(args, rank, world, local):
+    from moe_dispatch.routing import WORKLOADS
+    from moe_dispatch.graphs import capture_forward
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    workload = WORKLOADS[args.workload]
+    block, x = build_block(workload, device, seed_offset=rank)
+    tokens = workload.tokens
+    stream = torch.cuda.current_stream(device)
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            block(x)
+        graph, graph_out = capture_forward(block, x)
+        for _ in range(max(args.warmup, 3)):
+            graph.replay()
+        torch.cuda.synchronize()
+
+        # -- timed region: K graph replays (inputs resident in HBM)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        local_ms = start.elapsed_time(end)
+        total_ms = max_over_ranks(local_ms, world, device)
+        ms_per_step = total_ms / args.steps
+        value = tokens * world / (total_ms / 1e3 / args.steps)
+
+        # -- per-kernel durations over K eager steps (same stream, CUDA events)
+        names = ("dispatch", "gemm1", "gemm2", "combine")
+        samples = {n: [] for n in names}
+        eager_start, eager_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        eager_start.record(stream)
+        per_step = []
+        for _ in range(args.steps):
+            events = {n: (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                      for n in names}
+            step_instrumented(block, x, events)
+            per_step.append(events)
+        eager_end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        for events in per_step:
+            for n in names:
+                samples[n].append(events[n][0].elapsed_time(events[n][1]))
+        eager_ms = max_over_ranks(eager_start.elapsed_time(eager_end), world, device) / args.steps
+
+        # -- end to end through the public API with host buffers
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty_like(x_host).pin_memory()
+        x_dev = torch.empty_like(x)
+        for _ in range(2):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(block(x_dev), non_blocking=True)
+        e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e2e_start.record(stream)
+        for _ in range(args.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(block(x_dev), non_blocking=True)
+        e2e_end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device) / args.steps
+        status = block.extension.device_status()
+
+    hbm_peak, tf_peak, tf_sustained, peak_kind = measured_peaks()
+    n = tokens * workload.topk
+    h, i = workload.hidden, workload.intermediate
+    gemm1_flops = 2.0 * n * h * 2 * i
+    gemm1_ms = statistics.mean(samples["gemm1"])
+    achieved_tflops = gemm1_flops / (gemm1_ms / 1e3) / 1e12
+    gemm2_ms = statistics.mean(samples["gemm2"])
+    dispatch_bytes = tokens * h * 2 + n * h * 2 + n * 8
+    combine_bytes = n * h * 2 + tokens * h * 2 + n * 8
+    dispatch_ms = statistics.mean(samples["dispatch"])
+    combine_ms = statistics.mean(samples["combine"])
+    dc_gbs = (dispatch_bytes + combine_bytes) / ((dispatch_ms + combine_ms) / 1e3) / 1e9
+    traffic = profiled_traffic("grouped_gemm_kernel<true>")
+
+    result = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,1/fan_in) weights)",
+        "config": {
+            "workload": f"{workload.name}: T={tokens}/GPU H={h} I={i} E={workload.experts} "
+                        f"top{workload.topk}, fp32 router, bf16 experts",
+            "tokens_per_gpu": tokens, "hidden": h, "intermediate": i,
+            "experts": workload.experts, "topk": workload.topk,
+            "parallelism": "replicas" if world > 1 else "single GPU",
+            "timing": "CUDA graph replay of one block forward per step",
+            "l2": "inputs larger than L2 (2.8 GB of expert weights streamed per step)",
+        },
+        "eager_ms_per_step": round(eager_ms, 4),
+        "stage_ms": {"dispatch": round(dispatch_ms, 4), "gate_up_swiglu_gemm": round(gemm1_ms, 4),
+                     "down_gemm": round(gemm2_ms, 4), "combine": round(combine_ms, 4)},
+        "dispatch_combine_gbs": round(dc_gbs, 1),
+        "dispatch_combine_frac_of_hbm": round(dc_gbs / hbm_peak, 4),
+        "roofline": {
+            "kernel": "grouped_gemm_kernel<true> (gate/up + SwiGLU, tcgen05)",
+            "bound": "tensor",
+            "achieved": round(achieved_tflops, 1),
+            "peak": tf_peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved_tflops / tf_peak, 4),
+            "peak_kind": f"{peak_kind} burst bf16 (cuBLAS)",
+            "flops_per_launch": gemm1_flops,
+            "traffic": traffic,
+        },
+        "e2e": {
+            "value": round(tokens * world / (e2e_ms / 1e3), 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+            "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+        },
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(workload, block, x, args.cpu_sample_tokens)
+    return result
+
+
+# --------------------------------------------------------- CPU port (oracle)
+def cpu_sample(workload, weights, x, bias, tokens):
+    from oracle import moe_oracle as oracle
+
+    t0 = time.perf_counter()
+    oracle.block_forward(x[:tokens], weights.router, bias, weights.gate_up, weights.down,
+                         workload.topk)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(workload, block, x, sample_tokens):
+    from oracle import moe_oracle as oracle
+    from moe_dispatch.layer import MoEWeights
+
+    weights = MoEWeights(block.router_weight.cpu(), block.gate_up_weight.cpu(),
+                         block.down_weight.cpu())
+    xs = x[:sample_tokens].cpu()
+    bias = block.routing_bias.cpu()
+    seconds = cpu_sample(workload, weights, xs, bias, sample_tokens)
+    return {"value": round(sample_tokens / seconds, 2), "unit": "tokens/s",
+            "cores": oracle.num_threads(), "kind": "port",
+            "sample": f"{sample_tokens} tokens of the workload through the C oracle "
+                      f"(route, dispatch, grouped GEMMs, SwiGLU, combine), {seconds:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    from oracle import moe_oracle as oracle
+    from moe_dispatch.routing import WORKLOADS, block_input, block_weights
+
+    workload = WORKLOADS[args.workload]
+    weights, bias = block_weights(workload)
+    x = block_input(workload, tokens=args.cpu_sample_tokens)
+    for _ in range(args.warmup):
+        cpu_sample(workload, weights, x, bias, args.cpu_sample_tokens)
+    times = [cpu_sample(workload, weights, x, bias, args.cpu_sample_tokens)
+             for _ in range(args.steps)]
+    seconds = sum(times) / len(times)
+    value = args.cpu_sample_tokens / seconds
+    return {
+        "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(seconds * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{workload.name}: H={workload.hidden} I={workload.intermediate} "
+                               f"E={workload.experts} top{workload.topk}",
+                   "sample_tokens_per_step": args.cpu_sample_tokens},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": oracle.num_threads(),
+                         "kind": "port",
+                         "sample": f"{args.cpu_sample_tokens} tokens per step through the C "
+                                   "restatement of the reference's path"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    rank, world, local = dist_info()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps(run_reference(args, rank, world)), flush=True)
+        return 0
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    try:
+        result = run_ours(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,535 @@
+// Persistent grouped GEMM on 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the reference's expert stage (src/moe_dispatch/layer.py:159-182):
+// grouped_linear over packed rows (experts.py:21-35, Triton in
+// _triton_gemm.py:16-104) followed by swiglu_out (csrc/dispatch.cu:277-323).
+//
+// For expert e, packed rows [offsets[e], offsets[e+1]) are multiplied by the
+// expert's K-major weight block:
+//   plain :  out[r, c] = bf16( sum_k a[r,k] * w[e, c, k] )
+//   swiglu:  g = bf16(a[r].w[e,c]),  u = bf16(a[r].w[e,I+c]),  out = bf16(silu(g)*u)
+// The bf16 rounding of g and u reproduces the reference's materialised bf16
+// projection before its SwiGLU kernel, so fusing does not change results.
+//
+// Structure (one CTA per SM, 192 threads):
+//   warp 0       TMA producer: A tile 128x64 and B tile 256x64 (two 128-row
+//                boxes) per stage, 128-byte swizzle, 4 stages of 48 KiB.
+//   warp 1       TMEM allocator and single-thread MMA issuer:
+//                tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, fp32
+//                accumulators in TMEM, two 256-column buffers so the epilogue
+//                of one tile overlaps the main loop of the next.
+//   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, SwiGLU or cast,
+//                masked 16-byte stores (rows past the expert's end are skipped).
+// Tiles are scheduled on the device from `offsets` (no host sync): expert by
+// expert, and inside an expert n-tile by n-tile over its m-tiles, so the CTAs
+// in flight share the expert's A rows and stream each B tile once.
+//
+// Every mbarrier wait is bounded (globaltimer); when one runs out the kernel
+// records an error in its status word, stops issuing, waits (bounded) for its
+// copies and MMAs in flight, frees its TMEM and returns.
+#include "common.cuh"
+#include "launch.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+namespace moe {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBN = 256;
+constexpr int kBK = 64;
+constexpr int kUmmaK = 16;
+constexpr int kStages = 4;
+constexpr int kTileABytes = kBM * kBK * 2;
+constexpr int kTileBBytes = kBN * kBK * 2;
+constexpr int kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kBoxRows = 128;
+constexpr int kBoxBytes = kBoxRows * kBK * 2;
+constexpr int kTmemCols = 2 * kBN;
+constexpr int kThreads = 192;
+constexpr int kEpilogueThreads = 128;
+constexpr int kMaxExperts = 1024;
+constexpr uint64_t kWaitLimitNs = 4000000000ull;   // a wait that takes 4 s is an error
+constexpr uint64_t kDrainLimitNs = 200000000ull;   // bounded drain after an error
+
+constexpr int kBarrierBytes = (2 * kStages + 5) * 8;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + (kMaxExperts + 1) * 4;
+
+enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1 };
+
+__device__ int32_t g_gemm_status;
+
+struct GemmParams {
+    const int32_t* offsets;
+    __nv_bfloat16* out;
+    int64_t ldo;         // output row stride in elements
+    int n_out;           // output columns (intermediate for SwiGLU)
+    int k_dim;
+    int experts;
+    int n_tiles;         // output column tiles
+    int b_rows;          // weight rows per expert (2*I for SwiGLU, N otherwise)
+    int up_offset;       // row offset of the "up" half inside an expert (SwiGLU)
+};
+
+// ---------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+__device__ __forceinline__ void record_status(int32_t code) { atomicCAS(&g_gemm_status, 0, code); }
+
+// Bounded wait for the phase of `bar` with the given parity.  Returns false
+// when the CTA is aborting (another role gave up) or this wait ran out.
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                       uint64_t limit_ns) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_timer();
+    for (uint32_t i = 1;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 0) {
+            if (*abort_flag) return false;
+            if (global_timer() - start > limit_ns) {
+                record_status(kStatusWaitTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// K-major operand, 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes
+// apart (SBO); the leading offset is unused for this layout (encoded as 1).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+    return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+           (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor: D fp32, A and B bf16, both K-major, M x N.
+constexpr uint32_t make_idesc(int m, int n) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float round_bf16(float v) {
+    return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// Tile t -> (expert, m-tile, n-tile).  Tiles are ordered by expert; inside an
+// expert by n-tile, then m-tile.
+__device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int experts, int n_tiles,
+                                            int& e, int& m, int& n) {
+    const int q = t / n_tiles;
+    int lo = 0, hi = experts - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (mt_prefix[mid] <= q) lo = mid;
+        else hi = mid - 1;
+    }
+    e = lo;
+    const int mt = mt_prefix[e + 1] - mt_prefix[e];
+    const int local = t - mt_prefix[e] * n_tiles;
+    n = local / mt;
+    m = local - n * mt;
+}
+
+template <bool kSwiglu>
+__global__ void __launch_bounds__(kThreads, 1)
+grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                    const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tmem_full = empty + kStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
+    const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+
+    // m-tiles per expert -> exclusive prefix (warp 0).
+    if (warp == 0) {
+        int carry = 0;
+        for (int e0 = 0; e0 < p.experts; e0 += 32) {
+            const int e = e0 + lane;
+            int mt = 0;
+            if (e < p.experts) {
+                const int rows = p.offsets[e + 1] - p.offsets[e];
+                mt = rows > 0 ? (rows + kBM - 1) / kBM : 0;
+            }
+            int inclusive = mt;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+                if (lane >= off) inclusive += y;
+            }
+            if (e < p.experts) mt_prefix[e] = carry + inclusive - mt;
+            carry += __shfl_sync(0xffffffffu, inclusive, 31);
+        }
+        if (lane == 0) mt_prefix[p.experts] = carry;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int s = 0; s < kStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int a = 0; a < 2; ++a) {
+                mbar_init(&tmem_full[a], 1);
+                mbar_init(&tmem_empty[a], kEpilogueThreads);
+            }
+            mbar_init(drain, 1);
+            *abort_flag = 0;
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = mt_prefix[p.experts] * p.n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0;            // stages armed at least once
+            uint32_t last_parity = 0;      // parity of each stage's latest arm
+            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+                int e, m, n;
+                decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+                const int row0 = p.offsets[e] + m * kBM;
+                const int brow = e * p.b_rows + n * kOutTile;
+                const int brow2 = kSwiglu ? brow + p.up_offset : brow + kBoxRows;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* sa = tiles + stage * kStageBytes;
+                    uint8_t* sb = sa + kTileABytes;
+                    mbar_expect_tx(&full[stage], kStageBytes);
+                    tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
+                    tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow);
+                    tma_load_2d(sb + kBoxBytes, &tmap_b, &full[stage], kb * kBK, brow2);
+                    armed |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag) {
+                // Let every copy this thread started land before the CTA exits.
+                for (int s = 0; s < kStages; ++s)
+                    if (armed & (1u << s)) {
+                        volatile int never = 0;
+                        mbar_wait(&full[s], (last_parity >> s) & 1u, &never, kDrainLimitNs);
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            constexpr uint32_t idesc = make_idesc(kBM, kBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool issued = false;
+            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * kBN;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(tiles + stage * kStageBytes);
+                    const uint32_t b_addr = a_addr + kTileABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k)
+                        umma_bf16(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
+                                  smem_desc_sw128(b_addr + k * kUmmaK * 2), idesc,
+                                  (kb | k) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit(&empty[stage]);
+                    if (++stage == kStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit(&tmem_full[acc]);
+            }
+            if (*abort_flag && issued) {
+                // Wait for the MMAs in flight before TMEM is released.
+                umma_commit(drain);
+                volatile int never = 0;
+                mbar_wait(drain, 0, &never, kDrainLimitNs);
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        int local = 0;
+        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+            int e, m, n;
+            decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
+            tc_fence_after();
+            const int64_t row = static_cast<int64_t>(p.offsets[e]) + m * kBM + quarter * 32 + lane;
+            const bool valid = row < p.offsets[e + 1];
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+            __nv_bfloat16* dst_row = p.out + row * p.ldo;
+#pragma unroll 1
+            for (int c = 0; c < kOutTile; c += 32) {
+                uint32_t v[32];
+                uint32_t outw[16];
+                if constexpr (kSwiglu) {
+                    uint32_t u[32];
+                    tmem_ld32(taddr + c, v);
+                    tmem_ld32(taddr + kBN / 2 + c, u);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float a2[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float g = round_bf16(__uint_as_float(v[2 * j + h]));
+                            const float up = round_bf16(__uint_as_float(u[2 * j + h]));
+                            a2[h] = (g / (1.0f + expf(-g))) * up;
+                        }
+                        outw[j] = pack_bf16x2(a2[0], a2[1]);
+                    }
+                } else {
+                    tmem_ld32(taddr + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        outw[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                }
+                if (valid) {
+                    const int col0 = n * kOutTile + c;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (col0 + q * 8 + 8 <= p.n_out)
+                            *reinterpret_cast<uint4*>(dst_row + col0 + q * 8) =
+                                make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols));
+    }
+}
+
+// ------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult query;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &query) ==
+                cudaSuccess &&
+            query == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// Row-major bf16 matrix [rows, cols], boxes of 128 rows x 64 columns, 128B swizzle.
+bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return false;
+    cuuint64_t dims[2] = {cols, rows};
+    cuuint64_t strides[1] = {cols * 2};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBoxRows)};
+    cuuint32_t elem_strides[2] = {1, 1};
+    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct DeviceInfo {
+    int sms = 0;
+    bool configured[2] = {false, false};
+};
+
+DeviceInfo& device_info(int device) {
+    static DeviceInfo infos[64];
+    return infos[device & 63];
+}
+
+}  // namespace
+
+cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
+                                int64_t rows, int64_t n_out, int64_t k_dim, int experts,
+                                bool swiglu, cudaStream_t stream, const char** error) {
+    *error = nullptr;
+    if (rows == 0 || experts == 0) return cudaSuccess;
+    if (experts > kMaxExperts) {
+        *error = "grouped GEMM supports at most 1024 experts";
+        return cudaErrorInvalidValue;
+    }
+    int device = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&device));
+    DeviceInfo& info = device_info(device);
+    if (info.sms == 0) MOE_CUDA_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
+    auto kernel = swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>;
+    if (!info.configured[swiglu]) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        info.configured[swiglu] = true;
+    }
+    const int64_t b_rows = swiglu ? 2 * n_out : n_out;
+    CUtensorMap map_a, map_b;
+    if (!make_tensor_map(&map_a, a, static_cast<uint64_t>(rows), static_cast<uint64_t>(k_dim)) ||
+        !make_tensor_map(&map_b, b, static_cast<uint64_t>(b_rows * experts), static_cast<uint64_t>(k_dim))) {
+        *error = "cuTensorMapEncodeTiled rejected an operand (pointer alignment or shape)";
+        return cudaErrorInvalidValue;
+    }
+    GemmParams p;
+    p.offsets = offsets;
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.ldo = n_out;
+    p.n_out = static_cast<int>(n_out);
+    p.k_dim = static_cast<int>(k_dim);
+    p.experts = experts;
+    const int out_tile = swiglu ? kBN / 2 : kBN;
+    p.n_tiles = static_cast<int>((n_out + out_tile - 1) / out_tile);
+    p.b_rows = static_cast<int>(b_rows);
+    p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
+    const int64_t max_tiles = ((rows + kBM - 1) / kBM + experts) * static_cast<int64_t>(p.n_tiles);
+    const int grid = static_cast<int>(max_tiles < info.sms ? max_tiles : info.sms);
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p);
+    return cudaGetLastError();
+}
+
+cudaError_t read_gemm_status(int32_t* code, bool clear) {
+    MOE_CUDA_TRY(cudaMemcpyFromSymbol(code, g_gemm_status, sizeof(int32_t)));
+    if (clear) {
+        const int32_t zero = 0;
+        MOE_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(int32_t)));
+    }
+    return cudaSuccess;
+}
+
+}  // namespace moe

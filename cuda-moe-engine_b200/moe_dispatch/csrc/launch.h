@@ -1,0 +1,40 @@
+// Host-side launchers shared between the kernel files and the C ABI layer.
+// Arguments are validated by the caller (capi.cu); these only enqueue work.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace moe {
+
+constexpr int kMaxTopk = 32;
+constexpr int kMaxRouteExperts = 256;
+constexpr int kMaxDispatchExperts = 512;
+constexpr int kDispatchChunk = 4096;  // assignments per dispatch-index CTA
+
+cudaError_t launch_router_logits(const void* x, const float* w, float* logits, int64_t tokens,
+                                 int64_t hidden, int experts, cudaStream_t stream);
+cudaError_t launch_topk(const float* logits, const float* bias, int32_t* ids32, int64_t* ids64,
+                        float* weights, int64_t tokens, int experts, int topk, cudaStream_t stream);
+
+int64_t dispatch_scratch_bytes(int64_t assignments, int experts);
+cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_t* counts,
+                            int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse,
+                            int64_t tokens, int64_t hidden, int topk, int experts,
+                            int64_t packed_rows, int alignment, int vector_bytes, int32_t* scratch,
+                            cudaStream_t stream);
+cudaError_t launch_combine(const void* expert_output, int dtype, const int32_t* inverse,
+                           const float* weights, void* output, int64_t tokens, int64_t hidden,
+                           int topk, int64_t packed_rows, int vector_bytes, cudaStream_t stream);
+cudaError_t launch_swiglu(const void* projection, int dtype, const int32_t* valid_rows,
+                          void* output, int64_t rows, int64_t width, int vector_bytes,
+                          cudaStream_t stream);
+
+// Grouped GEMMs on tcgen05 (gemm_sm100.cu).  `error` receives a message when
+// the returned status is not cudaSuccess because of a host-side check.
+cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
+                                int64_t rows, int64_t n_out, int64_t k_dim, int experts,
+                                bool swiglu, cudaStream_t stream, const char** error);
+cudaError_t read_gemm_status(int32_t* code, bool clear);
+
+}  // namespace moe

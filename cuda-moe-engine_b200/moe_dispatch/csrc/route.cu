@@ -1,0 +1,201 @@
+// Router: fp32 logits from bf16 tokens, then top-k + softmax (sm_100a).
+//
+// Reference behaviour (src/moe_dispatch/layer.py:122-139, csrc/dispatch.cu:325-376):
+//   logits = F.linear(x.float(), W)             (fp32)
+//   values = logits + bias                      (fp32 add)
+//   top-k of values, ties -> lower expert index
+//   weights = softmax(selected values)
+//
+// Logit order: each logit is one sequential fp32 FMA chain over h = 0..H-1
+// starting from +0.0f.  The CPU oracle uses the same chain, so the logits --
+// and hence the selected experts -- are bit-identical between the two.
+#include "common.cuh"
+#include "launch.h"
+
+#include <climits>
+
+namespace moe {
+namespace {
+
+constexpr int kRouteChunk = 32;  // hidden elements staged per step
+
+// Tiled SIMT GEMM: a CTA owns TT tokens x TE experts; each thread owns MT x ME
+// logits.  Every logit accumulates in h order, so tiling does not change its value.
+template <int TT, int TE, int MT, int ME>
+__global__ void __launch_bounds__((TT / MT) * (TE / ME))
+router_logits_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                     float* __restrict__ logits, int64_t tokens, int hidden, int experts) {
+    constexpr int kThreads = (TT / MT) * (TE / ME);
+    constexpr int kTx = TE / ME;
+    __shared__ float xs[kRouteChunk][TT + 4];
+    __shared__ __align__(16) float ws[kRouteChunk][TE + 4];
+
+    const int tid = threadIdx.x;
+    const int tx = tid % kTx, ty = tid / kTx;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
+    const int e0 = blockIdx.y * TE;
+
+    float acc[MT][ME];
+#pragma unroll
+    for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int j = 0; j < ME; ++j) acc[i][j] = 0.0f;
+
+    for (int h0 = 0; h0 < hidden; h0 += kRouteChunk) {
+        // x tile: TT rows x 32 columns, four 16-byte pieces per row.
+        for (int v = tid; v < TT * 4; v += kThreads) {
+            const int row = v >> 2, piece = v & 3;
+            const int64_t t = t0 + row;
+            const int h = h0 + piece * 8;
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (t < tokens && h < hidden)
+                raw = __ldg(reinterpret_cast<const uint4*>(x + t * hidden + h));
+            const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                xs[piece * 8 + 2 * q][row] = bf16_bits_to_f32(words[q] & 0xffffu);
+                xs[piece * 8 + 2 * q + 1][row] = bf16_bits_to_f32(words[q] >> 16);
+            }
+        }
+        // W tile: TE rows x 32 columns of fp32, eight 16-byte pieces per row.
+        for (int v = tid; v < TE * 8; v += kThreads) {
+            const int row = v >> 3, piece = v & 7;
+            const int e = e0 + row;
+            const int h = h0 + piece * 4;
+            float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < experts && h < hidden)
+                val = __ldg(reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + h));
+            ws[piece * 4 + 0][row] = val.x;
+            ws[piece * 4 + 1][row] = val.y;
+            ws[piece * 4 + 2][row] = val.z;
+            ws[piece * 4 + 3][row] = val.w;
+        }
+        __syncthreads();
+        const int steps = min(kRouteChunk, hidden - h0);
+        for (int kk = 0; kk < steps; ++kk) {
+            float xv[MT], wv[ME];
+#pragma unroll
+            for (int i = 0; i < MT; ++i) xv[i] = xs[kk][ty * MT + i];
+#pragma unroll
+            for (int j = 0; j < ME; ++j) wv[j] = ws[kk][tx * ME + j];
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+#pragma unroll
+                for (int j = 0; j < ME; ++j) acc[i][j] = fmaf(xv[i], wv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+        const int64_t t = t0 + ty * MT + i;
+        if (t >= tokens) continue;
+#pragma unroll
+        for (int j = 0; j < ME; ++j) {
+            const int e = e0 + tx * ME + j;
+            if (e < experts) logits[t * experts + e] = acc[i][j];
+        }
+    }
+}
+
+// One warp per token.  Lane l holds experts l, l+32, ... (VPL of them).  K
+// rounds of warp argmax under the order (value desc, index asc); the winner is
+// struck from its lane.  Softmax over the selected values: e_k = exp(v_k - v_0),
+// summed in k order, multiplied by 1/sum (for K = 2 this is the reference's
+// 1/(1+r), r/(1+r), dispatch.cu:366-374).
+template <int VPL>
+__global__ void __launch_bounds__(256)
+topk_softmax_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+                    int32_t* __restrict__ ids32, int64_t* __restrict__ ids64,
+                    float* __restrict__ weights, int64_t tokens, int experts, int topk) {
+    const int lane = threadIdx.x & 31;
+    const int64_t token = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (token >= tokens) return;  // uniform per warp
+
+    float v[VPL];
+    bool avail[VPL];
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+        const int e = lane + 32 * i;
+        avail[i] = e < experts;
+        v[i] = avail[i] ? logits[token * experts + e] + (bias ? bias[e] : 0.0f) : -INFINITY;
+    }
+    float mine = 0.0f, first = 0.0f;
+    int mine_id = 0;
+    for (int k = 0; k < topk; ++k) {
+        float bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int i = 0; i < VPL; ++i) {
+            if (avail[i] && (bi == INT_MAX || v[i] > bv)) {
+                bv = v[i];
+                bi = lane + 32 * i;
+            }
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < VPL; ++i)
+                if (lane + 32 * i == bi) avail[i] = false;
+        }
+        if (k == 0) first = bv;
+        if (lane == k) {
+            mine = bv;
+            mine_id = bi;
+        }
+    }
+    const float ex = lane < topk ? expf(mine - first) : 0.0f;
+    float total = 0.0f;
+    for (int k = 0; k < topk; ++k) total += __shfl_sync(0xffffffffu, ex, k);
+    const float inv = 1.0f / total;
+    if (lane < topk) {
+        const int64_t p = token * topk + lane;
+        ids32[p] = mine_id;
+        if (ids64) ids64[p] = mine_id;
+        weights[p] = ex * inv;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_router_logits(const void* x, const float* w, float* logits, int64_t tokens,
+                                 int64_t hidden, int experts, cudaStream_t stream) {
+    if (tokens == 0) return cudaSuccess;
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    if (experts <= 8) {
+        constexpr int TT = 32, TE = 8;
+        dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), 1);
+        router_logits_kernel<TT, TE, 1, 1><<<grid, (TT / 1) * (TE / 1), 0, stream>>>(
+            xb, w, logits, tokens, static_cast<int>(hidden), experts);
+    } else {
+        constexpr int TT = 64, TE = 64;
+        dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), (experts + TE - 1) / TE);
+        router_logits_kernel<TT, TE, 4, 4><<<grid, (TT / 4) * (TE / 4), 0, stream>>>(
+            xb, w, logits, tokens, static_cast<int>(hidden), experts);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const float* logits, const float* bias, int32_t* ids32, int64_t* ids64,
+                        float* weights, int64_t tokens, int experts, int topk, cudaStream_t stream) {
+    if (tokens == 0) return cudaSuccess;
+    const unsigned blocks = static_cast<unsigned>((tokens + 7) / 8);
+    if (experts <= 32)
+        topk_softmax_kernel<1><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+    else if (experts <= 64)
+        topk_softmax_kernel<2><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+    else if (experts <= 128)
+        topk_softmax_kernel<4><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+    else
+        topk_softmax_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+    return cudaGetLastError();
+}
+
+}  // namespace moe

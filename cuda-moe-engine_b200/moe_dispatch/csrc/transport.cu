@@ -1,0 +1,380 @@
+// Token transport: dispatch (index + pack), combine and the standalone SwiGLU.
+//
+// Dispatch replaces the reference's count_slots / offsets / pack / zero_padding
+// kernels (src/moe_dispatch/csrc/dispatch.cu:13-74, 194-275).  The reference
+// assigns slots with atomicAdd, so its order inside an expert changes from run
+// to run; here the order is the stable token-major order of p = t*K + k:
+//
+//   dispatch_index_kernel  one CTA per 4096 assignments.  match_any groups a
+//                          warp's assignments by expert, per-warp histograms
+//                          are scanned in warp order, so each assignment gets
+//                          its rank inside the chunk without atomics.  The last
+//                          CTA to finish (ticket in scratch) scans the per-chunk
+//                          counts into chunk bases, writes counts[E] and the
+//                          padded offsets[E+1].
+//   pack_kernel            one CTA per token: reads the x row once, writes it to
+//                          its K packed rows (16-byte vectors), writes slots and
+//                          inverse; E extra CTAs zero the padding rows.
+#include "common.cuh"
+#include "launch.h"
+
+namespace moe {
+namespace {
+
+constexpr int kIndexThreads = 1024;
+constexpr int kScratchHeader = 16;  // int32 words before the chunk table (ticket + pad)
+
+template <int BYTES> struct VecOf;
+template <> struct VecOf<16> { using T = uint4; };
+template <> struct VecOf<8> { using T = uint2; };
+template <> struct VecOf<4> { using T = uint32_t; };
+template <> struct VecOf<2> { using T = uint16_t; };
+
+__global__ void __launch_bounds__(kIndexThreads)
+dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, int alignment,
+                      int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                      int32_t* __restrict__ slots, int32_t* __restrict__ scratch) {
+    extern __shared__ int32_t smem[];
+    int32_t* hist = smem;                     // [32][E] per-warp counts of this round
+    int32_t* base = smem + 32 * experts;      // [32][E] per-warp bases of this round
+    int32_t* running = smem + 64 * experts;   // [E] chunk-local running totals
+    __shared__ int is_last;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < 32 * experts; i += kIndexThreads) hist[i] = 0;
+    for (int i = tid; i < experts; i += kIndexThreads) running[i] = 0;
+    __syncthreads();
+
+    const int64_t chunk0 = static_cast<int64_t>(blockIdx.x) * kDispatchChunk;
+    const unsigned lanes_below = (1u << lane) - 1u;
+    for (int r = 0; r < kDispatchChunk / kIndexThreads; ++r) {
+        const int64_t p = chunk0 + r * kIndexThreads + tid;
+        const int e = p < n ? ids[p] : -1;
+        const bool valid = e >= 0 && e < experts;
+        const unsigned key = valid ? static_cast<unsigned>(e) : static_cast<unsigned>(experts + lane);
+        const unsigned peers = __match_any_sync(0xffffffffu, key);
+        const int rank = __popc(peers & lanes_below);
+        if (valid && rank == 0) hist[warp * experts + e] = __popc(peers);
+        __syncthreads();
+        for (int x = tid; x < experts; x += kIndexThreads) {
+            int run = running[x];
+            for (int w = 0; w < 32; ++w) {
+                const int c = hist[w * experts + x];
+                base[w * experts + x] = run;
+                hist[w * experts + x] = 0;
+                run += c;
+            }
+            running[x] = run;
+        }
+        __syncthreads();
+        if (p < n) slots[p] = valid ? base[warp * experts + e] + rank : -1;
+    }
+
+    int32_t* ticket = scratch;
+    int32_t* chunk_table = scratch + kScratchHeader;  // [chunks][E]
+    for (int x = tid; x < experts; x += kIndexThreads)
+        chunk_table[static_cast<int64_t>(blockIdx.x) * experts + x] = running[x];
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) is_last = atomicAdd(ticket, 1) == static_cast<int>(gridDim.x) - 1;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+
+    for (int x = tid; x < experts; x += kIndexThreads) {
+        int run = 0;
+        for (unsigned c = 0; c < gridDim.x; ++c) {
+            int32_t* cell = chunk_table + static_cast<int64_t>(c) * experts + x;
+            const int v = __ldcg(cell);
+            *cell = run;  // becomes the chunk's base for this expert
+            run += v;
+        }
+        counts[x] = run;
+        running[x] = alignment > 1 ? (run + alignment - 1) / alignment * alignment : run;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int per = (experts + 31) / 32;
+        const int start = min(experts, lane * per), end = min(experts, start + per);
+        int local = 0;
+        for (int x = start; x < end; ++x) local += running[x];
+        int inclusive = local;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+            if (lane >= off) inclusive += y;
+        }
+        int run = inclusive - local;
+        for (int x = start; x < end; ++x) {
+            offsets[x] = run;
+            run += running[x];
+        }
+        if (lane == 31) offsets[experts] = inclusive;
+        if (lane == 0) *ticket = 0;  // ready for the next call
+    }
+}
+
+template <typename V>
+__global__ void __launch_bounds__(256)
+pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
+            const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
+            const int32_t* __restrict__ chunk_table, int32_t* __restrict__ slots,
+            int32_t* __restrict__ inverse, V* __restrict__ packed, int64_t tokens, int topk,
+            int experts, int64_t row_vecs, int64_t packed_rows) {
+    __shared__ int64_t dest[kMaxTopk];
+    const int64_t t = blockIdx.x;
+    if (t < tokens) {
+        if (threadIdx.x < topk) {
+            const int64_t p = t * topk + threadIdx.x;
+            const int e = ids[p];
+            int64_t d = -1;
+            if (e >= 0 && e < experts) {
+                const int slot = chunk_table[(p / kDispatchChunk) * experts + e] + slots[p];
+                slots[p] = slot;
+                d = static_cast<int64_t>(offsets[e]) + slot;
+                if (d >= packed_rows) d = -1;
+            } else {
+                slots[p] = -1;
+            }
+            inverse[p] = static_cast<int32_t>(d);
+            dest[threadIdx.x] = d;
+        }
+        __syncthreads();
+        const V* src = x + t * row_vecs;
+        constexpr int kUnroll = 4;
+        for (int64_t c0 = threadIdx.x; c0 < row_vecs; c0 += kUnroll * blockDim.x) {
+            V v[kUnroll];
+#pragma unroll
+            for (int u = 0; u < kUnroll; ++u) {
+                const int64_t c = c0 + u * blockDim.x;
+                if (c < row_vecs) v[u] = __ldg(src + c);
+            }
+            for (int k = 0; k < topk; ++k) {
+                const int64_t d = dest[k];
+                if (d < 0) continue;
+                V* row = packed + d * row_vecs;
+#pragma unroll
+                for (int u = 0; u < kUnroll; ++u) {
+                    const int64_t c = c0 + u * blockDim.x;
+                    if (c < row_vecs) row[c] = v[u];
+                }
+            }
+        }
+    } else {
+        const int e = static_cast<int>(t - tokens);
+        const int64_t start = static_cast<int64_t>(offsets[e]) + counts[e];
+        int64_t end = offsets[e + 1];
+        if (end > packed_rows) end = packed_rows;
+        const V zero = {};
+        const int64_t total = (end - start) * row_vecs;
+        for (int64_t i = threadIdx.x; i < total; i += blockDim.x) packed[start * row_vecs + i] = zero;
+    }
+}
+
+// combine: out[t] = cast(sum_k (w[t,k] * f32(eo[row_k]))) with every product and
+// partial sum rounded to fp32 (__fmul_rn/__fadd_rn are never contracted to FMA).
+template <int DT, int VB>
+__global__ void __launch_bounds__(256)
+combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __restrict__ inverse,
+               const float* __restrict__ weights, typename VecOf<VB>::T* __restrict__ out,
+               int64_t tokens, int topk, int64_t row_vecs, int64_t packed_rows) {
+    using V = typename VecOf<VB>::T;
+    using E = Elem<DT>;
+    using T = typename E::T;
+    constexpr int N = VB / sizeof(T);
+    union Pun {
+        V v;
+        T e[N];
+    };
+    __shared__ int64_t rows[kMaxTopk];
+    __shared__ float ws[kMaxTopk];
+    const int64_t t = blockIdx.x;
+    if (threadIdx.x < topk) {
+        const int64_t p = t * topk + threadIdx.x;
+        const int32_t r = inverse[p];
+        rows[threadIdx.x] = (r >= 0 && r < packed_rows) ? r : -1;
+        ws[threadIdx.x] = weights[p];
+    }
+    __syncthreads();
+    for (int64_t c = threadIdx.x; c < row_vecs; c += blockDim.x) {
+        float acc[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) acc[i] = 0.0f;
+        for (int k = 0; k < topk; ++k) {
+            const int64_t r = rows[k];
+            if (r < 0) continue;
+            Pun in;
+            in.v = __ldg(eo + r * row_vecs + c);
+            const float wk = ws[k];
+#pragma unroll
+            for (int i = 0; i < N; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(wk, E::load(in.e[i])));
+        }
+        Pun o;
+#pragma unroll
+        for (int i = 0; i < N; ++i) o.e[i] = E::store(acc[i]);
+        out[t * row_vecs + c] = o.v;
+    }
+}
+
+// swiglu: out[r,c] = cast(silu(g) * u), g = f32(proj[r,c]), u = f32(proj[r,c+W]);
+// rows at or past *valid_rows are zero (dispatch.cu:277-292).
+template <int DT, int VB>
+__global__ void __launch_bounds__(256)
+swiglu_kernel(const typename VecOf<VB>::T* __restrict__ proj, const int32_t* __restrict__ valid_rows,
+              typename VecOf<VB>::T* __restrict__ out, int64_t rows, int64_t width_vecs) {
+    using V = typename VecOf<VB>::T;
+    using E = Elem<DT>;
+    using T = typename E::T;
+    constexpr int N = VB / sizeof(T);
+    union Pun {
+        V v;
+        T e[N];
+    };
+    const int64_t valid = *valid_rows;
+    const int64_t total = rows * width_vecs;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t r = i / width_vecs, c = i % width_vecs;
+        Pun o;
+        if (r >= valid) {
+#pragma unroll
+            for (int j = 0; j < N; ++j) o.e[j] = E::store(0.0f);
+        } else {
+            Pun g, u;
+            g.v = __ldg(proj + r * 2 * width_vecs + c);
+            u.v = __ldg(proj + r * 2 * width_vecs + width_vecs + c);
+#pragma unroll
+            for (int j = 0; j < N; ++j) {
+                const float gv = E::load(g.e[j]);
+                o.e[j] = E::store((gv / (1.0f + expf(-gv))) * E::load(u.e[j]));
+            }
+        }
+        out[i] = o.v;
+    }
+}
+
+template <int VB>
+cudaError_t launch_pack(const void* x, const int32_t* ids, const int32_t* counts,
+                        const int32_t* offsets, const int32_t* table, int32_t* slots,
+                        int32_t* inverse, void* packed, int64_t tokens, int topk, int experts,
+                        int64_t row_bytes, int64_t packed_rows, int alignment, cudaStream_t stream) {
+    using V = typename VecOf<VB>::T;
+    const int64_t row_vecs = row_bytes / VB;
+    const int64_t blocks = tokens + (alignment > 1 ? experts : 0);
+    if (blocks == 0) return cudaSuccess;
+    const int threads = row_vecs >= 256 ? 256 : 128;
+    pack_kernel<V><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
+        static_cast<const V*>(x), ids, counts, offsets, table, slots, inverse,
+        static_cast<V*>(packed), tokens, topk, experts, row_vecs, packed_rows);
+    return cudaGetLastError();
+}
+
+template <int DT, int VB>
+cudaError_t launch_combine_t(const void* eo, const int32_t* inverse, const float* weights,
+                             void* output, int64_t tokens, int64_t row_bytes, int topk,
+                             int64_t packed_rows, cudaStream_t stream) {
+    using V = typename VecOf<VB>::T;
+    const int64_t row_vecs = row_bytes / VB;
+    const int threads = row_vecs >= 256 ? 256 : 128;
+    combine_kernel<DT, VB><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
+        static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
+        row_vecs, packed_rows);
+    return cudaGetLastError();
+}
+
+template <int DT>
+cudaError_t launch_combine_dt(const void* eo, const int32_t* inverse, const float* weights,
+                              void* output, int64_t tokens, int64_t row_bytes, int topk,
+                              int64_t packed_rows, int vb, cudaStream_t stream) {
+    switch (vb) {
+        case 16: return launch_combine_t<DT, 16>(eo, inverse, weights, output, tokens, row_bytes, topk, packed_rows, stream);
+        case 8: return launch_combine_t<DT, 8>(eo, inverse, weights, output, tokens, row_bytes, topk, packed_rows, stream);
+        case 4: return launch_combine_t<DT, 4>(eo, inverse, weights, output, tokens, row_bytes, topk, packed_rows, stream);
+        default:
+            if constexpr (DT == kF32) return cudaErrorInvalidValue;
+            else return launch_combine_t<DT, 2>(eo, inverse, weights, output, tokens, row_bytes, topk, packed_rows, stream);
+    }
+}
+
+template <int DT, int VB>
+cudaError_t launch_swiglu_t(const void* proj, const int32_t* valid_rows, void* out, int64_t rows,
+                            int64_t width_bytes, cudaStream_t stream) {
+    using V = typename VecOf<VB>::T;
+    const int64_t width_vecs = width_bytes / VB;
+    const int64_t total = rows * width_vecs;
+    const int64_t blocks = (total + 255) / 256;
+    const unsigned grid = static_cast<unsigned>(blocks < 148 * 16 ? blocks : 148 * 16);
+    swiglu_kernel<DT, VB><<<grid, 256, 0, stream>>>(static_cast<const V*>(proj), valid_rows,
+                                                    static_cast<V*>(out), rows, width_vecs);
+    return cudaGetLastError();
+}
+
+template <int DT>
+cudaError_t launch_swiglu_dt(const void* proj, const int32_t* valid_rows, void* out, int64_t rows,
+                             int64_t width_bytes, int vb, cudaStream_t stream) {
+    switch (vb) {
+        case 16: return launch_swiglu_t<DT, 16>(proj, valid_rows, out, rows, width_bytes, stream);
+        case 8: return launch_swiglu_t<DT, 8>(proj, valid_rows, out, rows, width_bytes, stream);
+        case 4: return launch_swiglu_t<DT, 4>(proj, valid_rows, out, rows, width_bytes, stream);
+        default:
+            if constexpr (DT == kF32) return cudaErrorInvalidValue;
+            else return launch_swiglu_t<DT, 2>(proj, valid_rows, out, rows, width_bytes, stream);
+    }
+}
+
+}  // namespace
+
+int64_t dispatch_scratch_bytes(int64_t assignments, int experts) {
+    const int64_t chunks = assignments > 0 ? (assignments + kDispatchChunk - 1) / kDispatchChunk : 1;
+    return (kScratchHeader + chunks * experts) * static_cast<int64_t>(sizeof(int32_t));
+}
+
+cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_t* counts,
+                            int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse,
+                            int64_t tokens, int64_t hidden, int topk, int experts,
+                            int64_t packed_rows, int alignment, int vector_bytes, int32_t* scratch,
+                            cudaStream_t stream) {
+    const int64_t n = tokens * topk;
+    const int64_t chunks = n > 0 ? (n + kDispatchChunk - 1) / kDispatchChunk : 1;
+    const size_t smem = static_cast<size_t>(65 * experts) * sizeof(int32_t);
+    MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+    dispatch_index_kernel<<<static_cast<unsigned>(chunks), kIndexThreads, smem, stream>>>(
+        ids, n, experts, alignment, counts, offsets, slots, scratch);
+    MOE_CUDA_TRY(cudaGetLastError());
+    const int32_t* table = scratch + kScratchHeader;
+    const int64_t row_bytes = hidden * dtype_bytes(dtype);
+    switch (vector_bytes) {
+        case 16: return launch_pack<16>(x, ids, counts, offsets, table, slots, inverse, packed, tokens, topk, experts, row_bytes, packed_rows, alignment, stream);
+        case 8: return launch_pack<8>(x, ids, counts, offsets, table, slots, inverse, packed, tokens, topk, experts, row_bytes, packed_rows, alignment, stream);
+        case 4: return launch_pack<4>(x, ids, counts, offsets, table, slots, inverse, packed, tokens, topk, experts, row_bytes, packed_rows, alignment, stream);
+        default: return launch_pack<2>(x, ids, counts, offsets, table, slots, inverse, packed, tokens, topk, experts, row_bytes, packed_rows, alignment, stream);
+    }
+}
+
+cudaError_t launch_combine(const void* expert_output, int dtype, const int32_t* inverse,
+                           const float* weights, void* output, int64_t tokens, int64_t hidden,
+                           int topk, int64_t packed_rows, int vector_bytes, cudaStream_t stream) {
+    if (tokens == 0) return cudaSuccess;
+    const int64_t row_bytes = hidden * dtype_bytes(dtype);
+    switch (dtype) {
+        case kF32: return launch_combine_dt<kF32>(expert_output, inverse, weights, output, tokens, row_bytes, topk, packed_rows, vector_bytes, stream);
+        case kF16: return launch_combine_dt<kF16>(expert_output, inverse, weights, output, tokens, row_bytes, topk, packed_rows, vector_bytes, stream);
+        default: return launch_combine_dt<kBF16>(expert_output, inverse, weights, output, tokens, row_bytes, topk, packed_rows, vector_bytes, stream);
+    }
+}
+
+cudaError_t launch_swiglu(const void* projection, int dtype, const int32_t* valid_rows,
+                          void* output, int64_t rows, int64_t width, int vector_bytes,
+                          cudaStream_t stream) {
+    if (rows == 0 || width == 0) return cudaSuccess;
+    const int64_t width_bytes = width * dtype_bytes(dtype);
+    switch (dtype) {
+        case kF32: return launch_swiglu_dt<kF32>(projection, valid_rows, output, rows, width_bytes, vector_bytes, stream);
+        case kF16: return launch_swiglu_dt<kF16>(projection, valid_rows, output, rows, width_bytes, vector_bytes, stream);
+        default: return launch_swiglu_dt<kBF16>(projection, valid_rows, output, rows, width_bytes, vector_bytes, stream);
+    }
+}
+
+}  // namespace moe

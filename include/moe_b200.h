@@ -1,0 +1,133 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) MoE feed-forward library.
+ *
+ * Plain pointers and sizes; no torch types.  Every entry point:
+ *   - works on the calling thread's current CUDA device;
+ *   - takes caller-allocated inputs and outputs (it never allocates);
+ *   - enqueues asynchronously on `stream` (a cudaStream_t; NULL = legacy
+ *     default stream) and performs no host synchronisation, so it can be
+ *     captured in a CUDA graph;
+ *   - returns MOE_OK or an error code; moe_last_error() gives the message
+ *     of the calling thread's last failure.
+ *
+ * The reference (AarushRathore1729/cuda-moe-engine) binds five torch
+ * functions through pybind (src/moe_dispatch/csrc/bindings.cpp:3-13).  Each
+ * of them maps to one entry point here, cited beside it; the others are the
+ * fused stages the reference runs through torch/cuBLAS/Triton.
+ *
+ * Element types: MOE_F32, MOE_F16, MOE_BF16.  Index tensors are int32,
+ * routing weights fp32, ids64 int64 -- the reference's dtypes.
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum moe_dtype { MOE_F32 = 0, MOE_F16 = 1, MOE_BF16 = 2 };
+
+enum moe_status {
+    MOE_OK = 0,
+    MOE_ERR_INVALID = 1,     /* bad shape, size, dtype or pointer alignment */
+    MOE_ERR_CUDA = 2,        /* a CUDA runtime call or kernel launch failed */
+    MOE_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+    MOE_ERR_DEVICE = 4       /* a kernel reported an error through its device status word */
+};
+
+/* ABI revision of this header. */
+int moe_abi_version(void);
+
+/* Message for the calling thread's last failing call ("" if none). */
+const char* moe_last_error(void);
+
+/* ---------------------------------------------------------------- routing */
+
+/* Replaces topk_route_out (src/moe_dispatch/csrc/dispatch.cu:378-402,
+ * bindings.cpp:13-14): top-k over logits + bias with ties to the lower expert
+ * index, softmax over the selected scores.  Lifts the reference's limits
+ * (topk 1..2, experts <= 64) to topk 1..32, experts 1..256. */
+int moe_topk_route(const float* logits, const float* bias, int32_t* ids32, int64_t* ids64,
+                   float* weights, int64_t tokens, int32_t experts, int32_t topk, void* stream);
+
+/* Replaces MoEBlock.route for implementation="cuda_fused"
+ * (src/moe_dispatch/layer.py:122-135): fp32 router logits from bf16 x
+ * (F.linear(x.float(), W), layer.py:123) -- each logit a sequential fp32 FMA
+ * chain over h = 0..H-1 -- written to `logits` [T,E], then moe_topk_route. */
+int moe_route(const void* x_bf16, const float* router_weight, const float* bias, float* logits,
+              int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens, int64_t hidden,
+              int32_t experts, int32_t topk, void* stream);
+
+/* --------------------------------------------------------------- transport */
+
+/* Device scratch (bytes) that moe_dispatch needs for `tokens*topk`
+ * assignments over `experts` experts. */
+int64_t moe_dispatch_scratch_bytes(int64_t tokens, int32_t topk, int32_t experts);
+
+/* Replaces dispatch_out (dispatch.cu:102-158, bindings.cpp:3-5) when
+ * alignment == 1 and dispatch_aligned_out (dispatch.cu:218-275,
+ * bindings.cpp:8-10) when alignment > 1.  Writes counts[E], offsets[E+1]
+ * (each expert's span rounded up to `alignment`), slots[T*K] (rank of each
+ * assignment inside its expert), inverse[T*K] (its packed row) and copies
+ * each x row to its packed rows; padding rows are zeroed.  The order inside
+ * an expert is the stable token-major order of p = t*K + k, deterministic
+ * from run to run.  Out-of-range ids get slot and inverse -1.
+ * `vectorized` != 0 selects the widest vector copies the row allows.
+ * `scratch` must hold moe_dispatch_scratch_bytes() bytes, zeroed once
+ * before its first use; the call leaves it ready for the next call. */
+int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* counts,
+                 int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse, int64_t tokens,
+                 int64_t hidden, int32_t topk, int32_t experts, int64_t packed_rows,
+                 int32_t alignment, int32_t vectorized, void* scratch, int64_t scratch_bytes,
+                 void* stream);
+
+/* Replaces combine_out (dispatch.cu:160-192, bindings.cpp:6-7):
+ * out[t] = cast(sum_k fp32(w[t,k] * fp32(eo[inverse[t,k]]))), the products
+ * rounded to fp32 and summed in k order (the PyTorch path's rounding,
+ * reference.py:67-76).  Rows outside [0, packed_rows) are skipped. */
+int moe_combine(const void* expert_output, int32_t dtype, const int32_t* inverse,
+                const float* weights, void* output, int64_t tokens, int64_t hidden, int32_t topk,
+                int64_t packed_rows, void* stream);
+
+/* ----------------------------------------------------------------- experts */
+
+/* Replaces swiglu_out (dispatch.cu:294-323, bindings.cpp:11):
+ * out[r,c] = cast(silu(fp32 proj[r,c]) * fp32 proj[r,c+width]) for
+ * r < *valid_rows (a device int32), zero for the other rows. */
+int moe_swiglu(const void* projection, int32_t dtype, const int32_t* valid_rows, void* output,
+               int64_t rows, int64_t width, void* stream);
+
+/* Replaces the gate/up grouped_linear plus swiglu_out of
+ * MoEBlock.experts_forward (layer.py:162-172; experts.py:21-35;
+ * _triton_gemm.py:16-104).  bf16 only.  For each expert e and packed row r in
+ * [offsets[e], offsets[e+1]):
+ *   g = bf16(packed[r] . gate_up[e, c]),  u = bf16(packed[r] . gate_up[e, I+c])
+ *   activated[r, c] = bf16(silu(g) * u)                      (c < intermediate)
+ * packed [rows, hidden], gate_up [experts, 2*intermediate, hidden],
+ * activated [rows, intermediate]; fp32 accumulation on tcgen05 tensor cores.
+ * hidden and intermediate must be multiples of 8.  Rows at or beyond
+ * offsets[experts] are not written. */
+int moe_grouped_gemm_swiglu(const void* packed, const void* gate_up, const int32_t* offsets,
+                            void* activated, int64_t rows, int64_t hidden, int64_t intermediate,
+                            int32_t experts, void* stream);
+
+/* Replaces the down grouped_linear of MoEBlock.experts_forward
+ * (layer.py:175-181): out[r] = bf16(a[r] . weight[e]^T) for r in expert e's
+ * rows.  a [rows, k_dim], weight [experts, n_cols, k_dim], out [rows, n_cols];
+ * bf16, n_cols and k_dim multiples of 8. */
+int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, void* out,
+                     int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts, void* stream);
+
+/* ------------------------------------------------------------ diagnostics */
+
+/* Reads (and with clear != 0 resets) the current device's status word, which
+ * kernels with bounded waits set when a wait runs out.  0 means no error. */
+int moe_device_status(int32_t* code, int32_t clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */
