@@ -79,17 +79,25 @@ int moe_route(const void* x_bf16, const float* router_weight, const float* bias,
               int32_t experts, int32_t topk, void* stream) {
     if (hidden < 8 || hidden % 8 || hidden > INT_MAX)
         return fail(MOE_ERR_INVALID, "hidden must be a positive multiple of 8");
-    if (tokens > 0 && (!x_bf16 || !router_weight || !logits))
-        return fail(MOE_ERR_INVALID, "x, router_weight and logits must be non-null");
+    if (tokens > 0 && (!x_bf16 || !router_weight))
+        return fail(MOE_ERR_INVALID, "x and router_weight must be non-null");
+    if (tokens > 0 && experts > moe::kRouterSlicedMaxExperts && !logits)
+        return fail(MOE_ERR_INVALID, "logits must be non-null for more than %d experts",
+                    moe::kRouterSlicedMaxExperts);
     if (tokens > 0 && (!aligned(x_bf16, 16) || !aligned(router_weight, 16)))
         return fail(MOE_ERR_INVALID, "x and router_weight must be 16-byte aligned");
     if (experts < 1 || experts > moe::kMaxRouteExperts)
         return fail(MOE_ERR_INVALID, "routing supports 1..%d experts", moe::kMaxRouteExperts);
     if (tokens < 0) return fail(MOE_ERR_INVALID, "tokens must be >= 0");
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t err = moe::launch_router_logits(x_bf16, router_weight, logits, tokens, hidden, experts, s);
-    if (err != cudaSuccess) return cuda_status(err, "moe_route (logits)");
-    return moe_topk_route(logits, bias, ids32, ids64, weights, tokens, experts, topk, stream);
+    if (topk < 1 || topk > moe::kMaxTopk || topk > experts)
+        return fail(MOE_ERR_INVALID, "topk must be in 1..min(experts, %d)", moe::kMaxTopk);
+    if (tokens > INT_MAX / experts || tokens * topk > INT_MAX)
+        return fail(MOE_ERR_INVALID, "shape exceeds int32 indexing capacity");
+    if (tokens > 0 && (!ids32 || !weights)) return fail(MOE_ERR_INVALID, "ids32 and weights must be non-null");
+    return cuda_status(moe::launch_route(x_bf16, router_weight, bias, logits, ids32, ids64, weights,
+                                         tokens, hidden, experts, topk,
+                                         static_cast<cudaStream_t>(stream)),
+                       "moe_route");
 }
 
 int64_t moe_dispatch_scratch_bytes(int64_t tokens, int32_t topk, int32_t experts) {

@@ -10,10 +10,15 @@ namespace moe {
 constexpr int kMaxTopk = 32;
 constexpr int kMaxRouteExperts = 256;
 constexpr int kMaxDispatchExperts = 512;
-constexpr int kDispatchChunk = 4096;  // assignments per dispatch-index CTA
+constexpr int kDispatchChunk = 1024;  // assignments per dispatch-index CTA (one per thread)
+constexpr int kRouterSlicedMaxExperts = 32;  // sliced-butterfly logit order up to here
 
 cudaError_t launch_router_logits(const void* x, const float* w, float* logits, int64_t tokens,
                                  int64_t hidden, int experts, cudaStream_t stream);
+// Logits + top-k + softmax; logits may be null for E <= 32 (then not written).
+cudaError_t launch_route(const void* x, const float* w, const float* bias, float* logits,
+                         int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens,
+                         int64_t hidden, int experts, int topk, cudaStream_t stream);
 cudaError_t launch_topk(const float* logits, const float* bias, int32_t* ids32, int64_t* ids64,
                         float* weights, int64_t tokens, int experts, int topk, cudaStream_t stream);
 

@@ -6,9 +6,12 @@
 //   top-k of values, ties -> lower expert index
 //   weights = softmax(selected values)
 //
-// Logit order: each logit is one sequential fp32 FMA chain over h = 0..H-1
-// starting from +0.0f.  The CPU oracle uses the same chain, so the logits --
-// and hence the selected experts -- are bit-identical between the two.
+// Logit order (the CPU oracle restates it, so logits -- and hence the selected
+// experts -- are bit-identical between the two):
+//   E <= 32: H is cut into 32 contiguous slices of L = 8*ceil(H/256) elements;
+//            each slice is a sequential fp32 FMA chain from +0.0f, and the 32
+//            partial sums are combined by a xor butterfly (off = 16..1).
+//   E >  32: one sequential fp32 FMA chain over h = 0..H-1 from +0.0f.
 #include "common.cuh"
 #include "launch.h"
 
@@ -97,6 +100,116 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     }
 }
 
+// K rounds of warp argmax over one value per lane (lane = expert, E <= 32),
+// ties to the lower index, then softmax over the selected values; lanes < K
+// write (ids, weight) of the k-th choice.
+__device__ __forceinline__ void warp_topk_one_per_lane(float v, bool avail, int lane, int topk,
+                                                       int64_t out, int32_t* __restrict__ ids32,
+                                                       int64_t* __restrict__ ids64,
+                                                       float* __restrict__ weights) {
+    float mine = 0.0f, first = 0.0f;
+    int mine_id = 0;
+    for (int k = 0; k < topk; ++k) {
+        float bv = avail ? v : -INFINITY;
+        int bi = avail ? lane : INT_MAX;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (bi == lane) avail = false;
+        if (k == 0) first = bv;
+        if (lane == k) {
+            mine = bv;
+            mine_id = bi;
+        }
+    }
+    const float ex = lane < topk ? expf(mine - first) : 0.0f;
+    float total = 0.0f;
+    for (int k = 0; k < topk; ++k) total += __shfl_sync(0xffffffffu, ex, k);
+    const float inv = 1.0f / total;
+    if (lane < topk) {
+        ids32[out + lane] = mine_id;
+        if (ids64) ids64[out + lane] = mine_id;
+        weights[out + lane] = ex * inv;
+    }
+}
+
+// Router for E <= 32, logits and top-k in one kernel: one warp per TW tokens.
+// Lane l owns hidden slice l and keeps TW x EMAX partial sums (sequential FMA
+// chains); the xor butterfly leaves every logit in every lane; lane e then
+// holds expert e's biased score for the warp top-k.
+template <int EMAX, int TW>
+__global__ void __launch_bounds__(256)
+router_fused_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                    const float* __restrict__ bias, float* __restrict__ logits,
+                    int32_t* __restrict__ ids32, int64_t* __restrict__ ids64,
+                    float* __restrict__ weights, int64_t tokens, int hidden, int experts,
+                    int topk) {
+    const int lane = threadIdx.x & 31;
+    const int64_t t0 = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * TW;
+    if (t0 >= tokens) return;  // uniform per warp
+    const int len = 8 * ((hidden + 255) / 256);
+    const int h0 = lane * len;
+    const int h1 = min(hidden, h0 + len);
+    float acc[TW][EMAX];
+#pragma unroll
+    for (int i = 0; i < TW; ++i)
+#pragma unroll
+        for (int e = 0; e < EMAX; ++e) acc[i][e] = 0.0f;
+
+    for (int h = h0; h < h1; h += 8) {
+        float xv[TW][8];
+#pragma unroll
+        for (int i = 0; i < TW; ++i) {
+            uint4 raw = make_uint4(0, 0, 0, 0);
+            if (t0 + i < tokens) raw = __ldg(reinterpret_cast<const uint4*>(x + (t0 + i) * hidden + h));
+            const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                xv[i][2 * q] = bf16_bits_to_f32(words[q] & 0xffffu);
+                xv[i][2 * q + 1] = bf16_bits_to_f32(words[q] >> 16);
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < EMAX; ++e) {
+            if (e >= experts) break;
+            const float4* wr = reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + h);
+            const float4 w0 = __ldg(wr), w1 = __ldg(wr + 1);
+            const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < TW; ++i)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[i][e] = fmaf(xv[i][j], wv[j], acc[i][e]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < TW; ++i)
+#pragma unroll
+        for (int e = 0; e < EMAX; ++e)
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                acc[i][e] = acc[i][e] + __shfl_xor_sync(0xffffffffu, acc[i][e], off);
+
+#pragma unroll
+    for (int i = 0; i < TW; ++i) {
+        const int64_t t = t0 + i;
+        if (t >= tokens) break;  // uniform per warp
+        float mine = 0.0f;
+#pragma unroll
+        for (int e = 0; e < EMAX; ++e)
+            if (e == lane) mine = acc[i][e];
+        const bool avail = lane < experts;
+        if (avail && logits) logits[t * experts + lane] = mine;
+        const float v = avail ? mine + (bias ? bias[lane] : 0.0f) : -INFINITY;
+        warp_topk_one_per_lane(v, avail, lane, topk, t * topk, ids32, ids64, weights);
+    }
+}
+
 // One warp per token.  Lane l holds experts l, l+32, ... (VPL of them).  K
 // rounds of warp argmax under the order (value desc, index asc); the winner is
 // struck from its lane.  Softmax over the selected values: e_k = exp(v_k - v_0),
@@ -168,19 +281,37 @@ topk_softmax_kernel(const float* __restrict__ logits, const float* __restrict__ 
 cudaError_t launch_router_logits(const void* x, const float* w, float* logits, int64_t tokens,
                                  int64_t hidden, int experts, cudaStream_t stream) {
     if (tokens == 0) return cudaSuccess;
-    const auto* xb = static_cast<const __nv_bfloat16*>(x);
-    if (experts <= 8) {
-        constexpr int TT = 32, TE = 8;
-        dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), 1);
-        router_logits_kernel<TT, TE, 1, 1><<<grid, (TT / 1) * (TE / 1), 0, stream>>>(
-            xb, w, logits, tokens, static_cast<int>(hidden), experts);
-    } else {
-        constexpr int TT = 64, TE = 64;
-        dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), (experts + TE - 1) / TE);
-        router_logits_kernel<TT, TE, 4, 4><<<grid, (TT / 4) * (TE / 4), 0, stream>>>(
-            xb, w, logits, tokens, static_cast<int>(hidden), experts);
-    }
+    constexpr int TT = 64, TE = 64;
+    dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), (experts + TE - 1) / TE);
+    router_logits_kernel<TT, TE, 4, 4><<<grid, (TT / 4) * (TE / 4), 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), w, logits, tokens, static_cast<int>(hidden), experts);
     return cudaGetLastError();
+}
+
+template <int EMAX, int TW>
+static cudaError_t launch_fused(const void* x, const float* w, const float* bias, float* logits,
+                                int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens,
+                                int64_t hidden, int experts, int topk, cudaStream_t stream) {
+    const int64_t warps = (tokens + TW - 1) / TW;
+    router_fused_kernel<EMAX, TW><<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(
+        static_cast<const __nv_bfloat16*>(x), w, bias, logits, ids32, ids64, weights, tokens,
+        static_cast<int>(hidden), experts, topk);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_route(const void* x, const float* w, const float* bias, float* logits,
+                         int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens,
+                         int64_t hidden, int experts, int topk, cudaStream_t stream) {
+    if (tokens == 0) return cudaSuccess;
+    if (experts <= 8)
+        return launch_fused<8, 4>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
+    if (experts <= 16)
+        return launch_fused<16, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
+    if (experts <= kRouterSlicedMaxExperts)
+        return launch_fused<32, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
+    cudaError_t err = launch_router_logits(x, w, logits, tokens, hidden, experts, stream);
+    if (err != cudaSuccess) return err;
+    return launch_topk(logits, bias, ids32, ids64, weights, tokens, experts, topk, stream);
 }
 
 cudaError_t launch_topk(const float* logits, const float* bias, int32_t* ids32, int64_t* ids64,

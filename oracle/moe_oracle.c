@@ -22,9 +22,9 @@
  *     k = 0..K-1, then one cast (reference.py:67-76; torch's CPU reduction
  *     over that axis is sequential).
  *
- * Router logits use one defined summation order -- a sequential fmaf chain
- * over h = 0..H-1 starting from +0.0f -- which the CUDA router reproduces, so
- * logits (and hence top-k ids) are bit-exact between the two.
+ * Router logits use a defined fp32 summation order (see oracle_router_logits)
+ * which the CUDA router reproduces, so logits (and hence top-k ids) are
+ * bit-exact between the two.
  *
  * Build: oracle/Makefile (gcc -O3 -mavx2 -mfma -fopenmp -ffp-contract=off).
  */
@@ -87,7 +87,36 @@ static inline int elem_bytes(int dtype) { return dtype == OR_F32 ? 4 : 2; }
 uint16_t oracle_f32_to_bf16(float f) { return f32_to_bf16(f); }
 uint16_t oracle_f32_to_f16(float f) { return f32_to_f16(f); }
 
-/* ---- router: layer.py:123 (F.linear(x.float(), router_weight)) ---- */
+/* ---- router: layer.py:123 (F.linear(x.float(), router_weight)) ----
+ *
+ * The fp32 summation order is part of the definition, so that the CUDA router
+ * reproduces every logit bit for bit:
+ *   experts <= 32: H is cut into 32 contiguous slices of L = 8*ceil(H/256)
+ *     elements (slice l = [l*L, min(H, (l+1)*L)), possibly empty); each slice
+ *     is a sequential fmaf chain from +0.0f; the 32 partial sums are combined
+ *     by a xor butterfly: for off = 16, 8, 4, 2, 1: p[l] = p[l] + p[l ^ off];
+ *     the logit is p[0] (every l ends with the same value).
+ *   experts > 32: one sequential fmaf chain over h = 0..H-1 from +0.0f. */
+
+#define OR_ROUTER_SLICED_MAX_EXPERTS 32
+
+static float dot_sliced(const uint16_t* xr, const float* wr, int hidden) {
+    float p[32];
+    const int len = 8 * ((hidden + 255) / 256);
+    for (int l = 0; l < 32; ++l) {
+        float acc = 0.0f;
+        const int h0 = l * len;
+        const int h1 = h0 + len < hidden ? h0 + len : hidden;
+        for (int h = h0; h < h1; ++h) acc = fmaf(bf16_to_f32(xr[h]), wr[h], acc);
+        p[l] = acc;
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        float q[32];
+        for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+        memcpy(p, q, sizeof(p));
+    }
+    return p[0];
+}
 
 int oracle_router_logits(const uint16_t* x_bf16, const float* w, int64_t tokens, int hidden,
                          int experts, float* logits) {
@@ -98,7 +127,11 @@ int oracle_router_logits(const uint16_t* x_bf16, const float* w, int64_t tokens,
         for (int e = 0; e < experts; ++e) {
             const float* wr = w + (int64_t)e * hidden;
             float acc = 0.0f;
-            for (int h = 0; h < hidden; ++h) acc = fmaf(bf16_to_f32(xr[h]), wr[h], acc);
+            if (experts <= OR_ROUTER_SLICED_MAX_EXPERTS) {
+                acc = dot_sliced(xr, wr, hidden);
+            } else {
+                for (int h = 0; h < hidden; ++h) acc = fmaf(bf16_to_f32(xr[h]), wr[h], acc);
+            }
             logits[t * experts + e] = acc;
         }
     }

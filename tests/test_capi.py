@@ -31,7 +31,7 @@ def test_library_exports_every_declared_entry_point():
 def test_abi_version_and_scratch_query():
     lib = load_library()
     assert lib.moe_abi_version() == 1
-    assert lib.moe_dispatch_scratch_bytes(4096, 8, 64) == (16 + 8 * 64) * 4
+    assert lib.moe_dispatch_scratch_bytes(4096, 8, 64) == (16 + 32 * 64) * 4
     assert lib.moe_dispatch_scratch_bytes(0, 2, 8) == (16 + 8) * 4
     assert lib.moe_dispatch_scratch_bytes(-1, 2, 8) == -1
 

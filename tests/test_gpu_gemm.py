@@ -78,7 +78,8 @@ def test_plain_grouped_gemm_matches_oracle(ext, counts, k_dim, n_cols):
     used = int(offsets[-1])
     assert_gemm_close(got, a, w, offsets, what="plain")
     expected = oracle.grouped_gemm(a, w, offsets)
-    assert float((got[:used] != expected[:used]).float().mean()) < 0.02
+    if used:
+        assert float((got[:used] != expected[:used]).float().mean()) < 0.02
     # torch fp32 reference of the same op
     for e in range(len(counts)):
         lo, hi = int(offsets[e]), int(offsets[e + 1])
