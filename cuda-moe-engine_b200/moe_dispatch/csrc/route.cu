@@ -8,9 +8,11 @@
 //
 // Logit order (the CPU oracle restates it, so logits -- and hence the selected
 // experts -- are bit-identical between the two):
-//   E <= 32: H is cut into 32 contiguous slices of L = 8*ceil(H/256) elements;
-//            each slice is a sequential fp32 FMA chain from +0.0f, and the 32
-//            partial sums are combined by a xor butterfly (off = 16..1).
+//   E <= 32: slice l (l = 0..31) holds the elements h with (h / 8) mod 32 == l;
+//            each slice is a sequential fp32 FMA chain in increasing h from
+//            +0.0f, and the 32 partial sums are combined by a xor butterfly
+//            (off = 16..1).  Lane l owns slice l, so each warp load is 512
+//            contiguous bytes.
 //   E >  32: one sequential fp32 FMA chain over h = 0..H-1 from +0.0f.
 #include "common.cuh"
 #include "launch.h"
@@ -140,9 +142,9 @@ __device__ __forceinline__ void warp_topk_one_per_lane(float v, bool avail, int 
 }
 
 // Router for E <= 32, logits and top-k in one kernel: one warp per TW tokens.
-// Lane l owns hidden slice l and keeps TW x EMAX partial sums (sequential FMA
-// chains); the xor butterfly leaves every logit in every lane; lane e then
-// holds expert e's biased score for the warp top-k.
+// Lane l owns hidden slice l (8-element runs 256 apart) and keeps TW x EMAX
+// partial sums (sequential FMA chains); the xor butterfly leaves every logit in
+// every lane; lane e then holds expert e's biased score for the warp top-k.
 template <int EMAX, int TW>
 __global__ void __launch_bounds__(256)
 router_fused_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
@@ -153,16 +155,13 @@ router_fused_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict
     const int lane = threadIdx.x & 31;
     const int64_t t0 = ((static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5) * TW;
     if (t0 >= tokens) return;  // uniform per warp
-    const int len = 8 * ((hidden + 255) / 256);
-    const int h0 = lane * len;
-    const int h1 = min(hidden, h0 + len);
     float acc[TW][EMAX];
 #pragma unroll
     for (int i = 0; i < TW; ++i)
 #pragma unroll
         for (int e = 0; e < EMAX; ++e) acc[i][e] = 0.0f;
 
-    for (int h = h0; h < h1; h += 8) {
+    for (int h = 8 * lane; h < hidden; h += 256) {
         float xv[TW][8];
 #pragma unroll
         for (int i = 0; i < TW; ++i) {

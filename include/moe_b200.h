@@ -56,9 +56,9 @@ int moe_topk_route(const float* logits, const float* bias, int32_t* ids32, int64
  * (src/moe_dispatch/layer.py:122-135): fp32 router logits from bf16 x
  * (F.linear(x.float(), W), layer.py:123), then the selection of
  * moe_topk_route.  The fp32 summation order of a logit is fixed: for
- * experts <= 32, 32 contiguous slices of L = 8*ceil(H/256) elements, each a
- * sequential FMA chain, combined by a xor butterfly (off = 16, 8, 4, 2, 1);
- * for more experts, one sequential FMA chain over h.  `logits` [T,E] receives
+ * experts <= 32, 32 slices (slice l = the h with (h/8) mod 32 == l), each a
+ * sequential FMA chain in increasing h, combined by a xor butterfly
+ * (off = 16, 8, 4, 2, 1); for more experts, one sequential FMA chain over h.  `logits` [T,E] receives
  * the logits; it may be NULL when experts <= 32.  hidden % 8 == 0. */
 int moe_route(const void* x_bf16, const float* router_weight, const float* bias, float* logits,
               int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens, int64_t hidden,

@@ -91,23 +91,23 @@ uint16_t oracle_f32_to_f16(float f) { return f32_to_f16(f); }
  *
  * The fp32 summation order is part of the definition, so that the CUDA router
  * reproduces every logit bit for bit:
- *   experts <= 32: H is cut into 32 contiguous slices of L = 8*ceil(H/256)
- *     elements (slice l = [l*L, min(H, (l+1)*L)), possibly empty); each slice
- *     is a sequential fmaf chain from +0.0f; the 32 partial sums are combined
- *     by a xor butterfly: for off = 16, 8, 4, 2, 1: p[l] = p[l] + p[l ^ off];
- *     the logit is p[0] (every l ends with the same value).
+ *   experts <= 32: slice l (l = 0..31) holds the elements h with
+ *     (h / 8) mod 32 == l -- runs of 8 consecutive elements, 256 apart; each
+ *     slice is a sequential fmaf chain in increasing h from +0.0f; the 32
+ *     partial sums are combined by a xor butterfly: for off = 16, 8, 4, 2, 1:
+ *     p[l] = p[l] + p[l ^ off]; the logit is p[0] (every l ends equal).
  *   experts > 32: one sequential fmaf chain over h = 0..H-1 from +0.0f. */
 
 #define OR_ROUTER_SLICED_MAX_EXPERTS 32
 
 static float dot_sliced(const uint16_t* xr, const float* wr, int hidden) {
     float p[32];
-    const int len = 8 * ((hidden + 255) / 256);
     for (int l = 0; l < 32; ++l) {
         float acc = 0.0f;
-        const int h0 = l * len;
-        const int h1 = h0 + len < hidden ? h0 + len : hidden;
-        for (int h = h0; h < h1; ++h) acc = fmaf(bf16_to_f32(xr[h]), wr[h], acc);
+        for (int h0 = 8 * l; h0 < hidden; h0 += 256) {
+            const int h1 = h0 + 8 < hidden ? h0 + 8 : hidden;
+            for (int h = h0; h < h1; ++h) acc = fmaf(bf16_to_f32(xr[h]), wr[h], acc);
+        }
         p[l] = acc;
     }
     for (int off = 16; off > 0; off >>= 1) {
