@@ -33,6 +33,10 @@ SIGNATURES = {
         ctypes.c_int,
         [_P, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I64, _I32, _I32, _P, _I64, _P],
     ),
+    "moe_dispatch_no_alloc": (
+        ctypes.c_int,
+        [_P, _I32, _P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _I32, _I64, _I32, _I32, _P],
+    ),
     "moe_combine": (ctypes.c_int, [_P, _I32, _P, _P, _P, _I64, _I64, _I32, _I64, _P]),
     "moe_swiglu": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _I64, _P]),
     "moe_grouped_gemm_swiglu": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),

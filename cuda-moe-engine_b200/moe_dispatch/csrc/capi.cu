@@ -52,6 +52,10 @@ bool valid_dtype(int32_t dtype) { return dtype == MOE_F32 || dtype == MOE_F16 ||
 
 }  // namespace
 
+namespace moe {
+void set_last_error(const char* message) { g_last_error = message; }
+}  // namespace moe
+
 extern "C" {
 
 int moe_abi_version(void) { return 1; }

@@ -42,4 +42,7 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
                                 bool swiglu, cudaStream_t stream, const char** error);
 cudaError_t read_gemm_status(int32_t* code, bool clear);
 
+// Sets the calling thread's message returned by moe_last_error().
+void set_last_error(const char* message);
+
 }  // namespace moe

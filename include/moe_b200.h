@@ -87,6 +87,25 @@ int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* coun
                  int32_t alignment, int32_t vectorized, void* scratch, int64_t scratch_bytes,
                  void* stream);
 
+/* moe_dispatch for callers that cannot allocate device memory -- code inside a
+ * CUDA graph capture, hosts that forbid allocation after start-up, bindings
+ * that hold only raw device pointers.  No counterpart in the reference: its
+ * dispatch needs no scratch because its order is whatever atomics give.
+ * Same arguments and results as moe_dispatch, minus the scratch: that lives in
+ * a fixed array compiled into the library (256 KiB + 64 B on every GPU that
+ * loads it, until exit), which limits the size to
+ *   ceil(tokens * topk / 1024) * experts <= 65536
+ * (e.g. 262144 assignments over 256 experts); larger requests fail with
+ * MOE_ERR_INVALID.  Allocates nothing (no cudaMalloc/cudaFree).  The first
+ * call on a device looks up the array's device address; make it before any
+ * stream capture.  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+int moe_dispatch_no_alloc(const void* x, int32_t dtype, const int32_t* ids, int32_t* counts,
+                          int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse,
+                          int64_t tokens, int64_t hidden, int32_t topk, int32_t experts,
+                          int64_t packed_rows, int32_t alignment, int32_t vectorized,
+                          void* stream);
+
 /* Replaces combine_out (dispatch.cu:160-192, bindings.cpp:6-7):
  * out[t] = cast(sum_k fp32(w[t,k] * fp32(eo[inverse[t,k]]))), the products
  * rounded to fp32 and summed in k order (the PyTorch path's rounding,
