@@ -45,7 +45,10 @@ for _p in (ROOT / "cuda-moe-engine_b200", ROOT):
 import torch  # noqa: E402
 
 METRIC = "MoE-block tokens/s/GPU (H4096 I14336 E8 top2); dispatch+combine HBM GB/s"
-KERNELS_PER_STEP = 7  # route: logits + top-k; dispatch: index + pack; 2 GEMMs; combine
+def kernels_per_step(experts):
+    """Engine kernels per forward: route (1 fused up to 32 experts, else logits + top-k),
+    dispatch (index + pack), two grouped GEMMs, combine."""
+    return (1 if experts <= 32 else 2) + 2 + 2 + 1
 
 
 def parse_args():
@@ -55,7 +58,10 @@ def parse_args():
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["ours", "reference"], default="ours")
     parser.add_argument("--workload", default="mixtral")
-    parser.add_argument("--cpu-sample-tokens", type=int, default=64)
+    parser.add_argument("--cpu-sample-tokens", type=int, default=2048,
+                        help="tokens in the CPU-baseline sample of our arm (about 10 s)")
+    parser.add_argument("--reference-sample-tokens", type=int, default=256,
+                        help="tokens per step of --impl reference (about 1 s per step)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     return parser.parse_args()
 
@@ -69,7 +75,7 @@ def dist_info():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi samples (200 ms) of SM clock and throttle reasons while running."""
+    """nvidia-smi samples (every 20 ms) of SM clock and throttle reasons while running."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -84,7 +90,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.file, stderr=subprocess.DEVNULL)
             time.sleep(0.3)
         except OSError:
@@ -277,7 +283,7 @@ def run_ours(args, rank, world, local):
     dispatch_ms = statistics.mean(samples["dispatch"])
     combine_ms = statistics.mean(samples["combine"])
     dc_gbs = (dispatch_bytes + combine_bytes) / ((dispatch_ms + combine_ms) / 1e3) / 1e9
-    traffic = profiled_traffic("grouped_gemm_kernel<true>")
+    traffic = profiled_traffic("grouped_gemm_kernel<1>")
 
     result = {
         "metric": METRIC,
@@ -323,7 +329,7 @@ def run_ours(args, rank, world, local):
             "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
             "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
         },
-        "gpu_launches": KERNELS_PER_STEP * args.steps,
+        "gpu_launches": kernels_per_step(workload.experts) * args.steps,
         "clocks": clocks.summary(),
         "device_status": status,
     }
@@ -363,13 +369,13 @@ def run_reference(args, rank, world):
 
     workload = WORKLOADS[args.workload]
     weights, bias = block_weights(workload)
-    x = block_input(workload, tokens=args.cpu_sample_tokens)
+    sample = args.reference_sample_tokens
+    x = block_input(workload, tokens=sample)
     for _ in range(args.warmup):
-        cpu_sample(workload, weights, x, bias, args.cpu_sample_tokens)
-    times = [cpu_sample(workload, weights, x, bias, args.cpu_sample_tokens)
-             for _ in range(args.steps)]
+        cpu_sample(workload, weights, x, bias, sample)
+    times = [cpu_sample(workload, weights, x, bias, sample) for _ in range(args.steps)]
     seconds = sum(times) / len(times)
-    value = args.cpu_sample_tokens / seconds
+    value = sample / seconds
     return {
         "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -377,10 +383,10 @@ def run_reference(args, rank, world):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": f"{workload.name}: H={workload.hidden} I={workload.intermediate} "
                                f"E={workload.experts} top{workload.topk}",
-                   "sample_tokens_per_step": args.cpu_sample_tokens},
+                   "sample_tokens_per_step": sample},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": oracle.num_threads(),
                          "kind": "port",
-                         "sample": f"{args.cpu_sample_tokens} tokens per step through the C "
+                         "sample": f"{sample} tokens per step through the C "
                                    "restatement of the reference's path"},
         "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
