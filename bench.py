@@ -18,8 +18,11 @@ dispatch, gate/up GEMM with fused SwiGLU, down GEMM, combine.
   cpu_baseline  the CPU oracle (a C restatement of the reference's path) on a
              bounded token sample of the same workload, rank 0, N=1 only.
 
-With N > 1 (torchrun, one process per GPU) each rank runs the block on its
-own T tokens with its own weights (independent replicas, weak scaling).
+With N > 1 (torchrun, one process per GPU) the block runs expert-parallel:
+the E experts are sharded evenly over the N ranks (rank r owns E/N of them),
+each rank routes its own T tokens (weak scaling), and token rows travel to
+their experts' ranks and back with NCCL all-to-all (ExpertParallelMoEBlock,
+eager: the split sizes need one host sync per step).
 `--impl reference` times the CPU port of the reference's path instead (rank 0
 only; the other ranks exit without work).
 """
@@ -193,6 +196,131 @@ def max_over_ranks(value, world, device):
     t = torch.tensor([value], dtype=torch.float64, device=device)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return float(t.item())
+
+
+def build_ep_block(workload, device, rank, world):
+    """This rank's shard of the workload: all router rows, E/world experts, T tokens."""
+    from moe_dispatch.expert_parallel import ExpertParallelMoEBlock, expert_range
+    from moe_dispatch.layer import MoEConfig
+
+    w = workload
+    cfg = MoEConfig(w.hidden, w.intermediate, w.experts, w.topk)
+    first, local = expert_range(w.experts, world, rank)
+    g = torch.Generator(device=device).manual_seed(1000 + w.seed)
+    router = torch.randn(w.experts, w.hidden, device=device, generator=g) / w.hidden**0.5
+    gate_up = torch.empty(local, 2 * w.intermediate, w.hidden, device=device, dtype=torch.bfloat16)
+    down = torch.empty(local, w.hidden, w.intermediate, device=device, dtype=torch.bfloat16)
+    for e in range(local):
+        ge = torch.Generator(device=device).manual_seed(2000 + w.seed * 1000 + first + e)
+        gate_up[e] = (torch.randn(2 * w.intermediate, w.hidden, device=device, generator=ge)
+                      / w.hidden**0.5).to(torch.bfloat16)
+        down[e] = (torch.randn(w.hidden, w.intermediate, device=device, generator=ge)
+                   / w.intermediate**0.5).to(torch.bfloat16)
+    block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device)
+    gx = torch.Generator(device=device).manual_seed(3000 + w.seed * 1000 + rank)
+    x = torch.randn(w.tokens, w.hidden, device=device, generator=gx).to(torch.bfloat16)
+    return block, x
+
+
+def run_expert_parallel(args, rank, world, local):
+    from moe_dispatch.routing import WORKLOADS
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    workload = WORKLOADS[args.workload]
+    block, x = build_ep_block(workload, device, rank, world)
+    tokens = workload.tokens
+    stream = torch.cuda.current_stream(device)
+    names = ("exchange", "gemm1", "gemm2", "return")
+    with torch.inference_mode():
+        for _ in range(max(args.warmup, 3)):
+            block(x)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        per_step = []
+        barrier(world)
+        torch.cuda.synchronize()
+        with ClockSampler(local) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                events = {n: (torch.cuda.Event(enable_timing=True),
+                              torch.cuda.Event(enable_timing=True)) for n in names}
+                block(x, events=events)
+                per_step.append(events)
+            end.record(stream)
+            torch.cuda.synchronize()
+        barrier(world)
+        total_ms = max_over_ranks(start.elapsed_time(end), world, device)
+        stage = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in per_step) for n in names}
+        send_rows, recv_rows = block.last_split_sizes
+
+        x_host = x.cpu().pin_memory()
+        out_host = torch.empty_like(x_host).pin_memory()
+        x_dev = torch.empty_like(x)
+        for _ in range(2):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(block(x_dev), non_blocking=True)
+        e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(world)
+        torch.cuda.synchronize()
+        e2e_start.record(stream)
+        for _ in range(args.steps):
+            x_dev.copy_(x_host, non_blocking=True)
+            out_host.copy_(block(x_dev), non_blocking=True)
+        e2e_end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device) / args.steps
+        status = block.extension.device_status()
+
+    hbm_peak, tf_peak, _, peak_kind = measured_peaks()
+    h, i = workload.hidden, workload.intermediate
+    rows = sum(recv_rows)
+    gemm1_flops = 2.0 * rows * h * 2 * i
+    achieved = gemm1_flops / (stage["gemm1"] / 1e3) / 1e12
+    crossing = sum(v for r, v in enumerate(send_rows) if r != rank) * h * 2
+    ms_per_step = total_ms / args.steps
+    return {
+        "metric": METRIC,
+        "value": round(tokens * world / (ms_per_step / 1e3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,1/fan_in) weights)",
+        "config": {
+            "workload": f"{workload.name}: T={tokens}/GPU H={h} I={i} E={workload.experts} "
+                        f"top{workload.topk}, experts sharded {workload.experts // world}/GPU",
+            "tokens_per_gpu": tokens, "hidden": h, "intermediate": i,
+            "experts": workload.experts, "topk": workload.topk,
+            "parallelism": f"ep{world}",
+            "timing": "eager steps (one host sync per step for the all-to-all split sizes)",
+            "l2": "inputs larger than L2 (expert weights streamed per step)",
+        },
+        "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
+        "all_to_all_bytes_out_rank0": crossing,
+        "roofline": {
+            "kernel": "grouped_gemm_kernel<1> (gate/up + SwiGLU, tcgen05), rank 0",
+            "bound": "tensor", "achieved": round(achieved, 1), "peak": tf_peak,
+            "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
+            "peak_kind": f"{peak_kind} burst bf16 (cuBLAS)", "flops_per_launch": gemm1_flops,
+            "traffic": None,
+        },
+        "e2e": {
+            "value": round(tokens * world / (e2e_ms / 1e3), 1),
+            "unit": "tokens/s",
+            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+            "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+        },
+        "gpu_launches": (kernels_per_step(workload.experts) + 3) * args.steps,
+        "clocks": clocks.summary(),
+        "device_status": status,
+    }
 
 
 def run_ours(args, rank, world, local):
@@ -407,7 +535,7 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                              device_id=torch.device("cuda", local))
     try:
-        result = run_ours(args, rank, world, local)
+        result = (run_ours if world == 1 else run_expert_parallel)(args, rank, world, local)
         if rank == 0:
             print(json.dumps(result), flush=True)
     finally:

@@ -41,6 +41,10 @@ SIGNATURES = {
     "moe_swiglu": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _I64, _P]),
     "moe_grouped_gemm_swiglu": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "moe_grouped_gemm": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
+    "moe_ep_layout": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "moe_ep_regroup": (
+        ctypes.c_int, [_P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P]
+    ),
     "moe_device_status": (ctypes.c_int, [_P, _I32]),
 }
 
@@ -293,6 +297,35 @@ class Extension:
             a.data_ptr(), weight.data_ptr(), offsets.data_ptr(), out.data_ptr(), a.shape[0],
             n_cols, k_dim, experts,
         )
+
+    # ------------------------------------------------------- expert parallel
+    def ep_layout(self, counts, alignment, src_start, dst_start, offsets):
+        """Receive layout from counts[P, E_l] (see include/moe_b200.h, moe_ep_layout)."""
+        _require(counts.is_cuda and counts.dtype == torch.int32 and counts.dim() == 2,
+                 "expected int32 CUDA counts[P,E_l]")
+        ranks, experts = counts.shape
+        for tensor in (src_start, dst_start, offsets):
+            _check_cuda(tensor, counts, "ep_layout")
+        _require(src_start.numel() == ranks * experts and dst_start.numel() == ranks * experts
+                 and offsets.numel() == experts + 1, "incorrect layout buffers")
+        self._call(counts.device, self.lib.moe_ep_layout, counts.data_ptr(), ranks, experts,
+                   alignment, src_start.data_ptr(), dst_start.data_ptr(), offsets.data_ptr())
+
+    def ep_regroup(self, source, target, counts, src_start, dst_start, offsets, recv_rows,
+                   grouping):
+        """Received rows -> grouped (grouping=True) or grouped -> received order."""
+        _require(source.is_cuda and source.dim() == 2 and source.dtype in _DTYPE_CODES,
+                 "expected CUDA rows[R,H]")
+        for tensor in (target, counts, src_start, dst_start, offsets):
+            _check_cuda(tensor, source, "ep_regroup")
+        _require(target.dtype == source.dtype and target.shape[1] == source.shape[1],
+                 "row shape/dtype mismatch")
+        ranks, experts = counts.shape
+        grouped = target if grouping else source
+        self._call(source.device, self.lib.moe_ep_regroup, source.data_ptr(),
+                   _DTYPE_CODES[source.dtype], target.data_ptr(), counts.data_ptr(),
+                   src_start.data_ptr(), dst_start.data_ptr(), offsets.data_ptr(), ranks,
+                   experts, source.shape[1], recv_rows, grouped.shape[0], int(bool(grouping)))
 
     def device_status(self, clear=False):
         """Current device's kernel status word (0 = no bounded wait ran out)."""

@@ -218,6 +218,39 @@ int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, 
     return grouped_gemm_common(a, weight, offsets, out, rows, n_cols, k_dim, experts, false, stream);
 }
 
+int moe_ep_layout(const int32_t* counts, int32_t ranks, int32_t experts, int32_t alignment,
+                  int32_t* src_start, int32_t* dst_start, int32_t* offsets, void* stream) {
+    if (ranks < 1 || experts < 1 || static_cast<int64_t>(ranks) * experts > (1 << 20))
+        return fail(MOE_ERR_INVALID, "expert-parallel layout needs 1 <= ranks*experts <= 2^20");
+    if (alignment < 1 || alignment > 128) return fail(MOE_ERR_INVALID, "alignment must be 1..128");
+    if (!counts || !src_start || !dst_start || !offsets) return fail(MOE_ERR_INVALID, "null pointer");
+    return cuda_status(moe::launch_ep_layout(counts, ranks, experts, alignment, src_start, dst_start,
+                                             offsets, static_cast<cudaStream_t>(stream)),
+                       "moe_ep_layout");
+}
+
+int moe_ep_regroup(const void* from, int32_t dtype, void* to, const int32_t* counts,
+                   const int32_t* src_start, const int32_t* dst_start, const int32_t* offsets,
+                   int32_t ranks, int32_t experts, int64_t hidden, int64_t recv_rows,
+                   int64_t grouped_rows, int32_t grouping, void* stream) {
+    if (!valid_dtype(dtype)) return fail(MOE_ERR_INVALID, "unsupported dtype");
+    if (ranks < 1 || experts < 1 || hidden < 1 || recv_rows < 0 || grouped_rows < 0)
+        return fail(MOE_ERR_INVALID, "invalid expert-parallel regroup shape");
+    if (recv_rows > INT_MAX || grouped_rows > INT_MAX)
+        return fail(MOE_ERR_INVALID, "shape exceeds int32 indexing capacity");
+    if ((recv_rows > 0 || grouped_rows > 0) &&
+        (!from || !to || !counts || !src_start || !dst_start || !offsets))
+        return fail(MOE_ERR_INVALID, "null pointer");
+    const int elem = moe::dtype_bytes(dtype);
+    if (!aligned(from, elem) || !aligned(to, elem))
+        return fail(MOE_ERR_INVALID, "rows must be aligned to their element size");
+    const int vb = vector_bytes(hidden * elem, elem, {from, to});
+    return cuda_status(moe::launch_ep_regroup(from, to, counts, src_start, dst_start, offsets, ranks,
+                                              experts, hidden * elem, recv_rows, grouped_rows,
+                                              grouping != 0, vb, static_cast<cudaStream_t>(stream)),
+                       "moe_ep_regroup");
+}
+
 int moe_device_status(int32_t* code, int32_t clear) {
     if (!code) return fail(MOE_ERR_INVALID, "code must be non-null");
     return cuda_status(moe::read_gemm_status(code, clear != 0), "moe_device_status");

@@ -42,6 +42,16 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
                                 bool swiglu, cudaStream_t stream, const char** error);
 cudaError_t read_gemm_status(int32_t* code, bool clear);
 
+// Expert-parallel receive layout (ep.cu).
+cudaError_t launch_ep_layout(const int32_t* counts, int ranks, int experts, int alignment,
+                             int32_t* src_start, int32_t* dst_start, int32_t* offsets,
+                             cudaStream_t stream);
+cudaError_t launch_ep_regroup(const void* from, void* to, const int32_t* counts,
+                              const int32_t* src_start, const int32_t* dst_start,
+                              const int32_t* offsets, int ranks, int experts, int64_t row_bytes,
+                              int64_t recv_rows, int64_t grouped_rows, bool grouping,
+                              int vector_bytes, cudaStream_t stream);
+
 // Sets the calling thread's message returned by moe_last_error().
 void set_last_error(const char* message);
 

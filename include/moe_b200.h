@@ -143,6 +143,31 @@ int moe_grouped_gemm_swiglu(const void* packed, const void* gate_up, const int32
 int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, void* out,
                      int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts, void* stream);
 
+/* ------------------------------------------------------- expert parallel */
+
+/* Receive layout for expert parallelism (no counterpart in the reference,
+ * which is single-GPU, README.md:161-163).  counts[P][E_l] (device int32)
+ * holds how many rows each of P source ranks sent for each of this rank's
+ * E_l experts; they arrive source-major, each source's rows expert-major.
+ * Writes src_start[P][E_l] (first received row of each segment),
+ * dst_start[P][E_l] (its first row in the grouped layout) and
+ * offsets[E_l+1]: expert-major spans rounded up to `alignment`, source-major
+ * inside an expert -- which is the global token order, so grouped rows equal
+ * what a single GPU would pack for these experts. */
+int moe_ep_layout(const int32_t* counts, int32_t ranks, int32_t experts, int32_t alignment,
+                  int32_t* src_start, int32_t* dst_start, int32_t* offsets, void* stream);
+
+/* Moves rows between the received (source-major) and grouped (expert-major)
+ * layouts of moe_ep_layout: grouping != 0 copies received -> grouped and
+ * zeroes each expert's padding rows; grouping == 0 copies grouped rows back
+ * to received order (for the return exchange).  `from`/`to` are [rows, hidden]
+ * of `dtype`; recv_rows = sum(counts); grouped_rows = capacity of the grouped
+ * buffer (rows at or past it are skipped). */
+int moe_ep_regroup(const void* from, int32_t dtype, void* to, const int32_t* counts,
+                   const int32_t* src_start, const int32_t* dst_start, const int32_t* offsets,
+                   int32_t ranks, int32_t experts, int64_t hidden, int64_t recv_rows,
+                   int64_t grouped_rows, int32_t grouping, void* stream);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* Reads (and with clear != 0 resets) the current device's status word, which

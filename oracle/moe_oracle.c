@@ -392,6 +392,65 @@ int oracle_moe_tokens(const uint16_t* x, const int32_t* ids, const float* weight
     return failed ? OR_ENOMEM : OR_OK;
 }
 
+/* ---- expert-parallel receive layout.  No reference counterpart (the
+ *      reference is single-GPU, README.md:161-163); the layout is defined so
+ *      that grouped rows equal what one GPU packs for the same experts:
+ *      received rows are source-major, each source's rows expert-major; the
+ *      grouped layout is expert-major (spans rounded up to `alignment`) and
+ *      source-major inside an expert. ---- */
+
+int oracle_ep_layout(const int32_t* counts, int ranks, int experts, int alignment,
+                     int32_t* src_start, int32_t* dst_start, int32_t* offsets) {
+    if (ranks < 1 || experts < 1 || alignment < 1) return OR_EINVAL;
+    int32_t run = 0;
+    for (int p = 0; p < ranks; ++p)
+        for (int e = 0; e < experts; ++e) {
+            src_start[p * experts + e] = run;
+            run += counts[p * experts + e];
+        }
+    offsets[0] = 0;
+    for (int e = 0; e < experts; ++e) {
+        int32_t total = 0;
+        for (int p = 0; p < ranks; ++p) {
+            dst_start[p * experts + e] = offsets[e] + total;
+            total += counts[p * experts + e];
+        }
+        const int32_t span = alignment > 1 ? (total + alignment - 1) / alignment * alignment : total;
+        offsets[e + 1] = offsets[e] + span;
+    }
+    return OR_OK;
+}
+
+int oracle_ep_regroup(const void* from, int dtype, void* to, const int32_t* counts,
+                      const int32_t* src_start, const int32_t* dst_start, const int32_t* offsets,
+                      int ranks, int experts, int64_t hidden, int64_t grouped_rows, int grouping) {
+    if (ranks < 1 || experts < 1 || hidden < 1) return OR_EINVAL;
+    const size_t row_bytes = (size_t)hidden * elem_bytes(dtype);
+    for (int p = 0; p < ranks; ++p)
+        for (int e = 0; e < experts; ++e) {
+            const int i = p * experts + e;
+            for (int32_t r = 0; r < counts[i]; ++r) {
+                const int64_t recv_row = (int64_t)src_start[i] + r;
+                const int64_t grouped_row = (int64_t)dst_start[i] + r;
+                if (grouped_row >= grouped_rows) continue;
+                if (grouping)
+                    memcpy((char*)to + grouped_row * row_bytes, (const char*)from + recv_row * row_bytes,
+                           row_bytes);
+                else
+                    memcpy((char*)to + recv_row * row_bytes, (const char*)from + grouped_row * row_bytes,
+                           row_bytes);
+            }
+        }
+    if (grouping)
+        for (int e = 0; e < experts; ++e) {
+            int64_t filled = offsets[e];
+            for (int p = 0; p < ranks; ++p) filled += counts[p * experts + e];
+            for (int64_t r = filled; r < offsets[e + 1] && r < grouped_rows; ++r)
+                memset((char*)to + r * row_bytes, 0, row_bytes);
+        }
+    return OR_OK;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

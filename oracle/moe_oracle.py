@@ -45,6 +45,8 @@ def library():
         lib.oracle_swiglu.argtypes = [p, i32, i64, i64, i64, p]
         lib.oracle_grouped_gemm_bf16.argtypes = [p, p, p, i32, i64, i64, i64, p]
         lib.oracle_moe_tokens.argtypes = [p, p, p, p, p, i64, i32, i32, i32, p]
+        lib.oracle_ep_layout.argtypes = [p, i32, i32, i32, p, p, p]
+        lib.oracle_ep_regroup.argtypes = [p, i32, p, p, p, p, p, i32, i32, i64, i64, i32]
         lib.oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
         lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
@@ -227,6 +229,38 @@ def moe_tokens(x, ids, weights, gate_up, down):
         "oracle_moe_tokens",
     )
     return output
+
+
+def ep_layout(counts, alignment):
+    """Expert-parallel receive layout from counts[P, E_l] (see moe_oracle.c)."""
+    counts = counts.to(torch.int32).contiguous()
+    ranks, experts = counts.shape
+    src_start = torch.empty(ranks, experts, dtype=torch.int32)
+    dst_start = torch.empty(ranks, experts, dtype=torch.int32)
+    offsets = torch.empty(experts + 1, dtype=torch.int32)
+    _check(library().oracle_ep_layout(_ptr(counts), ranks, experts, alignment, _ptr(src_start),
+                                      _ptr(dst_start), _ptr(offsets)), "oracle_ep_layout")
+    return src_start, dst_start, offsets
+
+
+def ep_regroup(rows, counts, layout, grouped_rows=None, grouping=True):
+    """Received rows -> grouped (grouping) or grouped rows -> received order."""
+    counts = counts.to(torch.int32).contiguous()
+    src_start, dst_start, offsets = layout
+    ranks, experts = counts.shape
+    rows = rows.contiguous()
+    if grouping:
+        out_rows = int(offsets[-1]) if grouped_rows is None else grouped_rows
+        out = torch.full((out_rows, rows.shape[1]), float("nan"), dtype=rows.dtype)
+        capacity = out_rows
+    else:
+        out = torch.empty((int(counts.sum()), rows.shape[1]), dtype=rows.dtype)
+        capacity = rows.shape[0]
+    _check(library().oracle_ep_regroup(
+        _ptr(rows), _DTYPES[rows.dtype], _ptr(out), _ptr(counts), _ptr(src_start),
+        _ptr(dst_start), _ptr(offsets), ranks, experts, rows.shape[1], capacity, int(grouping),
+    ), "oracle_ep_regroup")
+    return out
 
 
 def block_forward(x, router_weight, bias, gate_up, down, topk, alignment=8):

@@ -1,0 +1,105 @@
+"""Expert-parallel kernels and block on the GPU.
+
+The layout/regroup kernels are checked bit for bit against the oracle's
+restatement.  The block with one rank must equal MoEBlock bit for bit (same
+rows per expert, same kernels).  With two or more GPUs, tests/ep_worker.py runs
+under torchrun and checks every rank's slice against the single-GPU block.
+"""
+
+import os
+import socket
+import subprocess
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+
+from oracle import moe_oracle as oracle
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="CUDA GPU required"),
+]
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def ext():
+    from moe_dispatch import get_extension
+
+    return get_extension()
+
+
+@pytest.mark.parametrize("ranks,experts,alignment", [(3, 5, 8), (1, 8, 8), (8, 32, 16), (2, 4, 1)])
+def test_layout_and_regroup_match_oracle(ext, ranks, experts, alignment):
+    g = torch.Generator().manual_seed(ranks * 100 + experts)
+    counts = torch.randint(0, 40, (ranks, experts), generator=g, dtype=torch.int32)
+    counts[0, 0] = 0
+    hidden = 136
+    layout = oracle.ep_layout(counts, alignment)
+    src_start = torch.empty(ranks, experts, dtype=torch.int32, device="cuda")
+    dst_start = torch.empty_like(src_start)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device="cuda")
+    cc = counts.cuda()
+    ext.ep_layout(cc, alignment, src_start, dst_start, offsets)
+    assert torch.equal(src_start.cpu(), layout[0])
+    assert torch.equal(dst_start.cpu(), layout[1])
+    assert torch.equal(offsets.cpu(), layout[2])
+    n_recv = int(counts.sum())
+    rows = torch.randn(n_recv, hidden, generator=g).to(torch.bfloat16)
+    grouped_rows = int(layout[2][-1]) + 3
+    grouped = torch.full((grouped_rows, hidden), 7.0, dtype=torch.bfloat16, device="cuda")
+    ext.ep_regroup(rows.cuda(), grouped, cc, src_start, dst_start, offsets, n_recv, True)
+    expected = oracle.ep_regroup(rows, counts, layout)
+    used = int(layout[2][-1])
+    assert torch.equal(grouped[:used].cpu(), expected)
+    back = torch.empty(n_recv, hidden, dtype=torch.bfloat16, device="cuda")
+    ext.ep_regroup(grouped, back, cc, src_start, dst_start, offsets, n_recv, False)
+    assert torch.equal(back.cpu(), rows)
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_single_rank_expert_parallel_block_equals_moeblock():
+    from moe_dispatch.expert_parallel import ExpertParallelMoEBlock
+    from moe_dispatch.layer import MoEBlock, MoEConfig, MoEWeights
+    from moe_dispatch.routing import BlockWorkload, block_input, block_weights
+
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_port()}", rank=0,
+                                world_size=1, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", 0))
+    try:
+        workload = BlockWorkload("ep1", 300, 256, 128, 16, 4, seed=9, router_std=0.02)
+        weights, bias = block_weights(workload)
+        cfg = MoEConfig(workload.hidden, workload.intermediate, workload.experts, workload.topk)
+        x = block_input(workload).cuda()
+        single = MoEBlock(cfg, weights=MoEWeights(weights.router.cuda(), weights.gate_up.cuda(),
+                                                  weights.down.cuda()))
+        single.routing_bias.copy_(bias)
+        ep = ExpertParallelMoEBlock(cfg, weights.router, weights.gate_up, weights.down,
+                                    routing_bias=bias)
+        expected = single(x).clone()
+        assert torch.equal(ep(x).clone(), expected)
+        assert torch.equal(ep(x).clone(), expected)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two or more GPUs")
+def test_multi_gpu_expert_parallel_matches_single_gpu():
+    gpus = min(torch.cuda.device_count(), 8)
+    gpus = 8 if gpus >= 8 else (4 if gpus >= 4 else 2)
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={gpus}",
+           "--master-addr=127.0.0.1", f"--master-port={_port()}", str(ROOT / "tests" / "ep_worker.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    result = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+    assert result.returncode == 0, result.stdout[-3000:] + result.stderr[-3000:]
