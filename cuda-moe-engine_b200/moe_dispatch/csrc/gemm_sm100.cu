@@ -439,6 +439,314 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
 }
 
+// ------------------------------------------------- CTA-pair (cta_group::2) variant
+//
+// Two CTAs of a cluster share one 256 x 256 tile: each CTA stages its own 128
+// rows of A and 128 rows of B (the gate half and the up half for SwiGLU,
+// otherwise two consecutive 128-row halves), 6 stages of 32 KiB.  The even
+// (leader) CTA issues tcgen05.mma.cta_group::2 with M=256, N=256, reading both
+// CTAs' shared memory; each CTA's TMEM receives the accumulator of its own 128
+// rows.  Both CTAs' TMA loads complete on the leader's full barrier (only the
+// leader arms its byte count); the leader's commits arrive on both CTAs'
+// barriers (multicast commit); both CTAs' epilogues release an accumulator on
+// the leader's barrier.  Per SM this halves the B bytes of the 1-CTA tile.
+
+constexpr int kPairStages = 6;
+constexpr int kPairTileABytes = kBM * kBK * 2;     // this CTA's 128 rows of A
+constexpr int kPairTileBBytes = kBoxRows * kBK * 2; // this CTA's 128 rows of B
+constexpr int kPairStageBytes = kPairTileABytes + kPairTileBBytes;
+constexpr int kPairBarrierBytes = (2 * kPairStages + 5) * 8;
+constexpr int kPairSmemBytes =
+    1024 + kPairStages * kPairStageBytes + kPairBarrierBytes + 16 + (kMaxExperts + 1) * 4;
+constexpr int kPairBM = 2 * kBM;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_count_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+
+// Address of the same shared variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t map_to_cta(uint32_t local_addr, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local_addr), "r"(rank));
+    return remote;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t leader_bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// Arrives (once) on the barrier at this shared offset in both CTAs of the pair
+// when every tcgen05 operation issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], %1;" ::"r"(smem_u32(bar)), "h"(static_cast<uint16_t>(0x3))
+        : "memory");
+}
+
+template <bool kSwiglu>
+__global__ void __launch_bounds__(kThreads, 1)
+grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* tiles = smem;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+    uint64_t* empty = full + kPairStages;
+    uint64_t* tmem_full = empty + kPairStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+    const bool leader = rank == 0;
+    const int pair = static_cast<int>(cluster_id_x());
+    const int pairs = static_cast<int>(cluster_count_x());
+    constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
+    const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+
+    // m-tiles (256 rows) per expert -> exclusive prefix (warp 0, both CTAs).
+    if (warp == 0) {
+        int carry = 0;
+        for (int e0 = 0; e0 < p.experts; e0 += 32) {
+            const int e = e0 + lane;
+            int mt = 0;
+            if (e < p.experts) {
+                const int rows = p.offsets[e + 1] - p.offsets[e];
+                mt = rows > 0 ? (rows + kPairBM - 1) / kPairBM : 0;
+            }
+            int inclusive = mt;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+                if (lane >= off) inclusive += y;
+            }
+            if (e < p.experts) mt_prefix[e] = carry + inclusive - mt;
+            carry += __shfl_sync(0xffffffffu, inclusive, 31);
+        }
+        if (lane == 0) mt_prefix[p.experts] = carry;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int s = 0; s < kPairStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int a = 0; a < 2; ++a) {
+                mbar_init(&tmem_full[a], 1);
+                mbar_init(&tmem_empty[a], 2 * kEpilogueThreads);
+            }
+            mbar_init(drain, 1);
+            *abort_flag = 0;
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int total_tiles = mt_prefix[p.experts] * p.n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer (both CTAs)
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, last_parity = 0;
+            for (int t = pair; t < total_tiles && !*abort_flag; t += pairs) {
+                int e, m, n;
+                decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+                const int row0 = p.offsets[e] + m * kPairBM + static_cast<int>(rank) * kBM;
+                const int brow0 = e * p.b_rows + n * kOutTile;
+                const int brow = kSwiglu ? brow0 + (leader ? 0 : p.up_offset)
+                                         : brow0 + static_cast<int>(rank) * kBoxRows;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t leader_full = map_to_cta(smem_u32(&full[stage]), 0);
+                    uint8_t* sa = tiles + stage * kPairStageBytes;
+                    if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+                    tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBK, row0);
+                    tma_load_2d_pair(sa + kPairTileABytes, &tmap_b, leader_full, kb * kBK, brow);
+                    armed |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag && leader) {
+                for (int s = 0; s < kPairStages; ++s)
+                    if (armed & (1u << s)) {
+                        volatile int never = 0;
+                        mbar_wait(&full[s], (last_parity >> s) & 1u, &never, kDrainLimitNs);
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ------------------------------------------------ MMA issuer (leader only)
+            constexpr uint32_t idesc = make_idesc(kPairBM, kBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int local = 0;
+            bool issued = false;
+            for (int t = pair; t < total_tiles && !*abort_flag; t += pairs, ++local) {
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * kBN;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(tiles + stage * kPairStageBytes);
+                    const uint32_t b_addr = a_addr + kPairTileABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k)
+                        umma_bf16_pair(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
+                                       smem_desc_sw128(b_addr + k * kUmmaK * 2), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit_pair(&empty[stage]);
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(&tmem_full[acc]);
+            }
+            if (*abort_flag && issued) {
+                umma_commit_pair(drain);
+                volatile int never = 0;
+                mbar_wait(drain, 0, &never, kDrainLimitNs);
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const uint32_t leader_empty0 = map_to_cta(smem_u32(&tmem_empty[0]), 0);
+        const uint32_t leader_empty1 = map_to_cta(smem_u32(&tmem_empty[1]), 0);
+        int local = 0;
+        for (int t = pair; t < total_tiles; t += pairs, ++local) {
+            int e, m, n;
+            decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
+            tc_fence_after();
+            const int64_t row = static_cast<int64_t>(p.offsets[e]) + m * kPairBM +
+                                static_cast<int>(rank) * kBM + quarter * 32 + lane;
+            const bool valid = row < p.offsets[e + 1];
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+            __nv_bfloat16* dst_row = p.out + row * p.ldo;
+#pragma unroll 1
+            for (int c = 0; c < kOutTile; c += 32) {
+                uint32_t v[32];
+                uint32_t outw[16];
+                if constexpr (kSwiglu) {
+                    uint32_t u[32];
+                    tmem_ld32(taddr + c, v);
+                    tmem_ld32(taddr + kBN / 2 + c, u);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        float a2[2];
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float g = round_bf16(__uint_as_float(v[2 * j + h]));
+                            const float up = round_bf16(__uint_as_float(u[2 * j + h]));
+                            a2[h] = (g / (1.0f + expf(-g))) * up;
+                        }
+                        outw[j] = pack_bf16x2(a2[0], a2[1]);
+                    }
+                } else {
+                    tmem_ld32(taddr + c, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        outw[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                }
+                if (valid) {
+                    const int col0 = n * kOutTile + c;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        if (col0 + q * 8 + 8 <= p.n_out)
+                            *reinterpret_cast<uint4*>(dst_row + col0 + q * 8) =
+                                make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still touch its memory
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols));
+    }
+}
+
 // ------------------------------------------------------------------ host side
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -471,12 +779,24 @@ bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 
 struct DeviceInfo {
     int sms = 0;
+    int pair_clusters = 0;
     bool configured[2] = {false, false};
+    bool pair_configured[2] = {false, false};
 };
 
 DeviceInfo& device_info(int device) {
     static DeviceInfo infos[64];
     return infos[device & 63];
+}
+
+// Tile shape selection: MOE_B200_GEMM_TILE=pair selects the CTA-pair kernel.
+// The default is the one-CTA tile: measured on B200 it is as fast or faster
+// for every block shape of the benchmark set except the fine-grained down
+// GEMM (6 % slower there), because the 256-row pair tile wastes more rows on
+// experts whose row count sits just above a multiple of the tile height.
+bool use_pair_tile(int64_t, int) {
+    const char* env = getenv("MOE_B200_GEMM_TILE");
+    return env && env[0] == 'p';
 }
 
 }  // namespace
@@ -494,11 +814,6 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     MOE_CUDA_TRY(cudaGetDevice(&device));
     DeviceInfo& info = device_info(device);
     if (info.sms == 0) MOE_CUDA_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
-    auto kernel = swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>;
-    if (!info.configured[swiglu]) {
-        MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        info.configured[swiglu] = true;
-    }
     const int64_t b_rows = swiglu ? 2 * n_out : n_out;
     CUtensorMap map_a, map_b;
     if (!make_tensor_map(&map_a, a, static_cast<uint64_t>(rows), static_cast<uint64_t>(k_dim)) ||
@@ -517,6 +832,43 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     p.n_tiles = static_cast<int>((n_out + out_tile - 1) / out_tile);
     p.b_rows = static_cast<int>(b_rows);
     p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
+
+    if (use_pair_tile(rows, experts)) {
+        auto kernel = swiglu ? grouped_gemm_pair_kernel<true> : grouped_gemm_pair_kernel<false>;
+        cudaLaunchConfig_t config = {};
+        cudaLaunchAttribute attribute[1];
+        attribute[0].id = cudaLaunchAttributeClusterDimension;
+        attribute[0].val.clusterDim.x = 2;
+        attribute[0].val.clusterDim.y = 1;
+        attribute[0].val.clusterDim.z = 1;
+        config.blockDim = dim3(kThreads);
+        config.dynamicSmemBytes = kPairSmemBytes;
+        config.stream = stream;
+        config.attrs = attribute;
+        config.numAttrs = 1;
+        if (!info.pair_configured[swiglu]) {
+            MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              kPairSmemBytes));
+            info.pair_configured[swiglu] = true;
+        }
+        if (info.pair_clusters == 0) {
+            config.gridDim = dim3(info.sms & ~1);
+            int clusters = 0;
+            MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kernel, &config));
+            info.pair_clusters = clusters > 0 ? clusters : info.sms / 2;
+        }
+        const int64_t max_tiles =
+            ((rows + kPairBM - 1) / kPairBM + experts) * static_cast<int64_t>(p.n_tiles);
+        const int64_t clusters = max_tiles < info.pair_clusters ? max_tiles : info.pair_clusters;
+        config.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+        return cudaLaunchKernelEx(&config, kernel, map_a, map_b, p);
+    }
+
+    auto kernel = swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>;
+    if (!info.configured[swiglu]) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        info.configured[swiglu] = true;
+    }
     const int64_t max_tiles = ((rows + kBM - 1) / kBM + experts) * static_cast<int64_t>(p.n_tiles);
     const int grid = static_cast<int>(max_tiles < info.sms ? max_tiles : info.sms);
     kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p);

@@ -25,6 +25,13 @@ pytestmark = [
 SENTINEL = -12345.0
 
 
+@pytest.fixture(autouse=True, params=["single", "pair"])
+def tile(request, monkeypatch):
+    """Run every test with the 128x256 one-CTA tile and the 256x256 CTA-pair tile."""
+    monkeypatch.setenv("MOE_B200_GEMM_TILE", request.param)
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def ext():
     from moe_dispatch import get_extension
