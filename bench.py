@@ -198,8 +198,16 @@ def max_over_ranks(value, world, device):
     return float(t.item())
 
 
+def ep_tokens_per_rank(workload, world):
+    """The expert-parallel configuration fixes T per step and splits it over the
+    ranks (strong scaling); the other workloads keep T tokens per GPU (weak)."""
+    if workload.name == "expert_parallel":
+        return workload.tokens // world, "strong"
+    return workload.tokens, "weak"
+
+
 def build_ep_block(workload, device, rank, world):
-    """This rank's shard of the workload: all router rows, E/world experts, T tokens."""
+    """This rank's shard of the workload: all router rows, E/world experts, its tokens."""
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock, expert_range
     from moe_dispatch.layer import MoEConfig
 
@@ -218,7 +226,8 @@ def build_ep_block(workload, device, rank, world):
                    / w.intermediate**0.5).to(torch.bfloat16)
     block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device)
     gx = torch.Generator(device=device).manual_seed(3000 + w.seed * 1000 + rank)
-    x = torch.randn(w.tokens, w.hidden, device=device, generator=gx).to(torch.bfloat16)
+    tokens, _ = ep_tokens_per_rank(w, world)
+    x = torch.randn(tokens, w.hidden, device=device, generator=gx).to(torch.bfloat16)
     return block, x
 
 
@@ -229,7 +238,7 @@ def run_expert_parallel(args, rank, world, local):
     torch.cuda.set_device(device)
     workload = WORKLOADS[args.workload]
     block, x = build_ep_block(workload, device, rank, world)
-    tokens = workload.tokens
+    tokens, scaling = ep_tokens_per_rank(workload, world)
     stream = torch.cuda.current_stream(device)
     names = ("exchange", "gemm1", "gemm2", "return")
     with torch.inference_mode():
@@ -289,7 +298,7 @@ def run_expert_parallel(args, rank, world, local):
         "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,1/fan_in) weights)",

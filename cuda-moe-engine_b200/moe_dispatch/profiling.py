@@ -2,6 +2,7 @@
 
     python -m moe_dispatch.profiling --workload mixtral --stage experts --iters 2
     python -m moe_dispatch.profiling --workload small --trace trace.json
+    python -m moe_dispatch.profiling --tile-sweep
 
 `--stage` runs one stage of the block `--iters` times after one untimed
 forward, so an ncu capture (`-k regex:<kernel> -s 1 -c 1`) sees a warm launch
@@ -69,6 +70,62 @@ def run_stage(block, x, stage, iters):
 
 
 @torch.inference_mode()
+def tile_sweep(cases=(("mixtral", 4096), ("fine_grained", 16384), ("expert_parallel", 8192),
+                      ("expert_parallel", 32768)), warmup=3, iters=10):
+    """Time both grouped GEMMs with the one-CTA and the CTA-pair tile (JSON lines)."""
+    import json
+    import os
+
+    previous = os.environ.get("MOE_B200_GEMM_TILE")
+    try:
+        for name, tokens in cases:
+            block, x = build(name, tokens=tokens)
+            block(x)
+            state = block.workspace(x)
+            t = state.transport
+            ext = block.extension
+            ids32, ids64, _ = block.route(x)
+            t.dispatch(x, ids32, ids64)
+            counts = t.counts.float().cpu()
+            cfg = block.config
+            n = tokens * cfg.topk
+            stages = {
+                "gate_up_swiglu": (lambda: ext.grouped_gemm_swiglu_out(
+                    t.packed, block.gate_up_weight, t.offsets, state.activated),
+                    2 * n * cfg.hidden * 2 * cfg.intermediate),
+                "down": (lambda: ext.grouped_gemm_out(
+                    state.activated, block.down_weight, t.offsets, state.expert_output),
+                    2 * n * cfg.intermediate * cfg.hidden),
+            }
+            for tile in ("single", "pair"):
+                os.environ["MOE_B200_GEMM_TILE"] = tile
+                for stage, (fn, flops) in stages.items():
+                    for _ in range(warmup):
+                        fn()
+                    torch.cuda.synchronize()
+                    start = torch.cuda.Event(enable_timing=True)
+                    end = torch.cuda.Event(enable_timing=True)
+                    start.record()
+                    for _ in range(iters):
+                        fn()
+                    end.record()
+                    torch.cuda.synchronize()
+                    ms = start.elapsed_time(end) / iters
+                    print(json.dumps({"workload": name, "tokens": tokens, "tile": tile,
+                                      "gemm": stage, "ms": round(ms, 4),
+                                      "tflops": round(flops / ms / 1e9, 1),
+                                      "rows_per_expert_mean": float(counts.mean()),
+                                      "rows_per_expert_max": float(counts.max())}), flush=True)
+            del block, x, state, t
+            torch.cuda.empty_cache()
+    finally:
+        if previous is None:
+            os.environ.pop("MOE_B200_GEMM_TILE", None)
+        else:
+            os.environ["MOE_B200_GEMM_TILE"] = previous
+
+
+@torch.inference_mode()
 def export_trace(block, x, destination, repeats=3):
     state = block.workspace(x)
     for _ in range(3):
@@ -103,7 +160,11 @@ def main():
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--experts", type=int, default=None)
     parser.add_argument("--trace", default=None)
+    parser.add_argument("--tile-sweep", action="store_true")
     args = parser.parse_args()
+    if args.tile_sweep:
+        tile_sweep()
+        return 0
     block, x = build(args.workload, tokens=args.tokens, experts=args.experts)
     if args.trace:
         print(export_trace(block, x, args.trace))
