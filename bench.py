@@ -66,6 +66,8 @@ def parse_args():
     parser.add_argument("--reference-sample-tokens", type=int, default=256,
                         help="tokens per step of --impl reference (about 1 s per step)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--ep-backend", choices=["p2p", "nccl"], default=None,
+                        help="expert-parallel exchange for N > 1 (default p2p up to 8 GPUs)")
     return parser.parse_args()
 
 
@@ -206,7 +208,7 @@ def ep_tokens_per_rank(workload, world):
     return workload.tokens, "weak"
 
 
-def build_ep_block(workload, device, rank, world):
+def build_ep_block(workload, device, rank, world, backend=None):
     """This rank's shard of the workload: all router rows, E/world experts, its tokens."""
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock, expert_range
     from moe_dispatch.layer import MoEConfig
@@ -224,7 +226,7 @@ def build_ep_block(workload, device, rank, world):
                       / w.hidden**0.5).to(torch.bfloat16)
         down[e] = (torch.randn(w.hidden, w.intermediate, device=device, generator=ge)
                    / w.intermediate**0.5).to(torch.bfloat16)
-    block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device)
+    block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device, backend=backend)
     gx = torch.Generator(device=device).manual_seed(3000 + w.seed * 1000 + rank)
     tokens, _ = ep_tokens_per_rank(w, world)
     x = torch.randn(tokens, w.hidden, device=device, generator=gx).to(torch.bfloat16)
@@ -237,31 +239,54 @@ def run_expert_parallel(args, rank, world, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     workload = WORKLOADS[args.workload]
-    block, x = build_ep_block(workload, device, rank, world)
+    block, x = build_ep_block(workload, device, rank, world, args.ep_backend)
     tokens, scaling = ep_tokens_per_rank(workload, world)
     stream = torch.cuda.current_stream(device)
     names = ("exchange", "gemm1", "gemm2", "return")
+    graphed = block.backend == "p2p"
     with torch.inference_mode():
         for _ in range(max(args.warmup, 3)):
             block(x)
         torch.cuda.synchronize()
+        barrier(world)
+        if graphed:  # no host sync in the p2p step: replay it as a CUDA graph
+            from moe_dispatch.graphs import capture_forward
+
+            graph, _ = capture_forward(block, x)
+            for _ in range(3):
+                graph.replay()
+            torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        per_step = []
         barrier(world)
         torch.cuda.synchronize()
         with ClockSampler(local) as clocks:
             start.record(stream)
             for _ in range(args.steps):
-                events = {n: (torch.cuda.Event(enable_timing=True),
-                              torch.cuda.Event(enable_timing=True)) for n in names}
-                block(x, events=events)
-                per_step.append(events)
+                if graphed:
+                    graph.replay()
+                else:
+                    block(x)
             end.record(stream)
             torch.cuda.synchronize()
         barrier(world)
         total_ms = max_over_ranks(start.elapsed_time(end), world, device)
+        # per-stage CUDA events over K eager steps
+        per_step = []
+        barrier(world)
+        torch.cuda.synchronize()
+        for _ in range(args.steps):
+            events = {n: (torch.cuda.Event(enable_timing=True),
+                          torch.cuda.Event(enable_timing=True)) for n in names}
+            block(x, events=events)
+            per_step.append(events)
+        torch.cuda.synchronize()
+        barrier(world)
         stage = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in per_step) for n in names}
-        send_rows, recv_rows = block.last_split_sizes
+        counts = block._transport[(x.shape[0], x.device)].counts.view(world, -1).sum(1).tolist()
+        send_rows = [int(c) for c in counts]
+        recv_rows = None
+        if block.backend == "nccl":
+            send_rows, recv_rows = block.last_split_sizes
 
         x_host = x.cpu().pin_memory()
         out_host = torch.empty_like(x_host).pin_memory()
@@ -284,11 +309,17 @@ def run_expert_parallel(args, rank, world, local):
 
     hbm_peak, tf_peak, _, peak_kind = measured_peaks()
     h, i = workload.hidden, workload.intermediate
-    rows = sum(recv_rows)
+    if recv_rows is None:  # p2p: the grouped span total on this rank
+        rows = int(block.exchange.state[4 + workload.experts + workload.experts // world].item())
+    else:
+        rows = sum(recv_rows)
     gemm1_flops = 2.0 * rows * h * 2 * i
     achieved = gemm1_flops / (stage["gemm1"] / 1e3) / 1e12
     crossing = sum(v for r, v in enumerate(send_rows) if r != rank) * h * 2
     ms_per_step = total_ms / args.steps
+    if graphed:
+        del graph
+    block.close()
     return {
         "metric": METRIC,
         "value": round(tokens * world / (ms_per_step / 1e3), 1),
@@ -308,7 +339,10 @@ def run_expert_parallel(args, rank, world, local):
             "tokens_per_gpu": tokens, "hidden": h, "intermediate": i,
             "experts": workload.experts, "topk": workload.topk,
             "parallelism": f"ep{world}",
-            "timing": "eager steps (one host sync per step for the all-to-all split sizes)",
+            "exchange": block.backend,
+            "timing": ("CUDA graph replay of one expert-parallel step (NVLink peer stores, no "
+                       "host sync)" if graphed else
+                       "eager steps (one host sync per step for the all-to-all split sizes)"),
             "l2": "inputs larger than L2 (expert weights streamed per step)",
         },
         "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
@@ -326,7 +360,7 @@ def run_expert_parallel(args, rank, world, local):
             "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
             "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
         },
-        "gpu_launches": (kernels_per_step(workload.experts) + 3) * args.steps,
+        "gpu_launches": (kernels_per_step(workload.experts) + (5 if graphed else 3)) * args.steps,
         "clocks": clocks.summary(),
         "device_status": status,
     }

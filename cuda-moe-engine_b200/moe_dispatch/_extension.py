@@ -45,6 +45,17 @@ SIGNATURES = {
     "moe_ep_regroup": (
         ctypes.c_int, [_P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P]
     ),
+    "moe_peer_alloc": (ctypes.c_int, [_I64, _P, _P]),
+    "moe_peer_open": (ctypes.c_int, [_P, _P]),
+    "moe_peer_close": (ctypes.c_int, [_P]),
+    "moe_peer_free": (ctypes.c_int, [_P]),
+    "moe_ep_p2p_region_bytes": (ctypes.c_int64, [_I32, _I32, _I64, _I64, _I64]),
+    "moe_ep_p2p_region_offset": (ctypes.c_int64, [_I32, _I32, _I64, _I64, _I64, _I32]),
+    "moe_ep_p2p_state_words": (ctypes.c_int64, [_I32, _I32]),
+    "moe_ep_p2p": (
+        ctypes.c_int,
+        [_I32, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P],
+    ),
     "moe_device_status": (ctypes.c_int, [_P, _I32]),
 }
 

@@ -13,6 +13,7 @@
 #include <climits>
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <string>
 
 namespace {
@@ -251,9 +252,97 @@ int moe_ep_regroup(const void* from, int32_t dtype, void* to, const int32_t* cou
                        "moe_ep_regroup");
 }
 
+int moe_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle) {
+    if (bytes < 1 || !ptr || !ipc_handle) return fail(MOE_ERR_INVALID, "invalid peer allocation");
+    void* p = nullptr;
+    cudaError_t err = cudaMalloc(&p, static_cast<size_t>(bytes));
+    if (err != cudaSuccess) return cuda_status(err, "moe_peer_alloc (cudaMalloc)");
+    err = cudaMemset(p, 0, static_cast<size_t>(bytes));
+    if (err == cudaSuccess)
+        err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(ipc_handle), p);
+    if (err != cudaSuccess) {
+        cudaFree(p);
+        return cuda_status(err, "moe_peer_alloc");
+    }
+    *ptr = p;
+    return MOE_OK;
+}
+
+int moe_peer_open(const void* ipc_handle, void** ptr) {
+    if (!ipc_handle || !ptr) return fail(MOE_ERR_INVALID, "null pointer");
+    cudaIpcMemHandle_t handle;
+    memcpy(&handle, ipc_handle, sizeof(handle));
+    return cuda_status(cudaIpcOpenMemHandle(ptr, handle, cudaIpcMemLazyEnablePeerAccess),
+                       "moe_peer_open");
+}
+
+int moe_peer_close(void* ptr) {
+    if (!ptr) return fail(MOE_ERR_INVALID, "null pointer");
+    return cuda_status(cudaIpcCloseMemHandle(ptr), "moe_peer_close");
+}
+
+int moe_peer_free(void* ptr) {
+    if (!ptr) return fail(MOE_ERR_INVALID, "null pointer");
+    return cuda_status(cudaFree(ptr), "moe_peer_free");
+}
+
+int64_t moe_ep_p2p_region_bytes(int32_t ranks, int32_t experts, int64_t hidden,
+                                int64_t grouped_rows, int64_t back_rows) {
+    if (ranks < 1 || ranks > moe::kEpP2pMaxRanks || experts < ranks || experts % ranks ||
+        hidden < 8 || hidden % 8 || grouped_rows < 0 || back_rows < 0)
+        return -1;
+    return moe::ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows);
+}
+
+int64_t moe_ep_p2p_region_offset(int32_t ranks, int32_t experts, int64_t hidden,
+                                 int64_t grouped_rows, int64_t back_rows, int32_t section) {
+    if (moe_ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows) < 0 ||
+        section < 0 || section > 1)
+        return -1;
+    return moe::ep_p2p_region_offset(ranks, experts, hidden, grouped_rows, back_rows, section);
+}
+
+int64_t moe_ep_p2p_state_words(int32_t ranks, int32_t experts) {
+    if (ranks < 1 || experts < ranks || experts % ranks) return -1;
+    return moe::ep_p2p_state_words(ranks, experts);
+}
+
+int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* regions,
+               int32_t* state, int32_t ranks, int32_t rank, int32_t experts, int32_t alignment,
+               int64_t hidden, int64_t grouped_rows, int64_t back_rows, int64_t timeout_ms,
+               void* stream) {
+    if (moe_ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows) < 0)
+        return fail(MOE_ERR_INVALID, "expert-parallel P2P: 1 <= ranks <= %d, experts a multiple "
+                                     "of ranks, hidden a multiple of 8", moe::kEpP2pMaxRanks);
+    if (rank < 0 || rank >= ranks) return fail(MOE_ERR_INVALID, "rank out of range");
+    if (experts > moe::kMaxRouteExperts)
+        return fail(MOE_ERR_INVALID, "expert-parallel P2P supports up to %d experts",
+                    moe::kMaxRouteExperts);
+    if (alignment < 1 || alignment > 128) return fail(MOE_ERR_INVALID, "alignment must be 1..128");
+    if (op < moe::kEpP2pCounts || op > moe::kEpP2pWaitReturn) return fail(MOE_ERR_INVALID, "bad op");
+    if (!regions || !state) return fail(MOE_ERR_INVALID, "null pointer");
+    for (int i = 0; i < ranks; ++i)
+        if (!regions[i] || !aligned(regions[i], 1024))
+            return fail(MOE_ERR_INVALID, "peer regions must be non-null and 1024-byte aligned");
+    if ((op == moe::kEpP2pCounts || op == moe::kEpP2pSend) && !aux)
+        return fail(MOE_ERR_INVALID, "counts / dispatch offsets required");
+    if ((op == moe::kEpP2pSend || op == moe::kEpP2pReturn) && (!rows || !aligned(rows, 16)))
+        return fail(MOE_ERR_INVALID, "rows must be non-null and 16-byte aligned");
+    if (timeout_ms < 1) return fail(MOE_ERR_INVALID, "timeout_ms must be >= 1");
+    return cuda_status(moe::launch_ep_p2p(op, rows, aux, regions, state, ranks, rank, experts,
+                                          alignment, hidden, grouped_rows, back_rows, timeout_ms,
+                                          static_cast<cudaStream_t>(stream)),
+                       "moe_ep_p2p");
+}
+
 int moe_device_status(int32_t* code, int32_t clear) {
     if (!code) return fail(MOE_ERR_INVALID, "code must be non-null");
-    return cuda_status(moe::read_gemm_status(code, clear != 0), "moe_device_status");
+    int32_t gemm = 0, ep = 0;
+    int status = cuda_status(moe::read_gemm_status(&gemm, clear != 0), "moe_device_status");
+    if (status != MOE_OK) return status;
+    status = cuda_status(moe::read_ep_status(&ep, clear != 0), "moe_device_status");
+    *code = gemm ? gemm : ep;
+    return status;
 }
 
 }  // extern "C"

@@ -52,6 +52,21 @@ cudaError_t launch_ep_regroup(const void* from, void* to, const int32_t* counts,
                               int64_t recv_rows, int64_t grouped_rows, bool grouping,
                               int vector_bytes, cudaStream_t stream);
 
+// Expert-parallel exchange over peer memory (ep_p2p.cu).
+constexpr int kEpP2pMaxRanks = 8;
+enum EpP2pOp { kEpP2pCounts = 0, kEpP2pSend = 1, kEpP2pWaitRows = 2, kEpP2pReturn = 3,
+               kEpP2pWaitReturn = 4 };
+int64_t ep_p2p_region_bytes(int ranks, int experts, int64_t hidden, int64_t grouped_rows,
+                            int64_t back_rows);
+int64_t ep_p2p_region_offset(int ranks, int experts, int64_t hidden, int64_t grouped_rows,
+                             int64_t back_rows, int section);
+int64_t ep_p2p_state_words(int ranks, int experts);
+cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* const* regions,
+                          int32_t* state, int ranks, int me, int experts, int alignment,
+                          int64_t hidden, int64_t grouped_rows, int64_t back_rows,
+                          int64_t timeout_ms, cudaStream_t stream);
+cudaError_t read_ep_status(int32_t* code, bool clear);
+
 // Sets the calling thread's message returned by moe_last_error().
 void set_last_error(const char* message);
 

@@ -20,12 +20,24 @@ Inside an expert, received rows are ordered by source rank, and ranks hold
 consecutive token ranges, so the grouped rows are exactly the rows a single GPU
 would pack: the output is bit-identical to MoEBlock on one GPU.
 
-Steps 3-4 need the split sizes on the host, so a forward synchronises once
-after the count exchange; the count, split and row-exchange helpers take any
-process group and tensors on any device (the gloo tests run them on CPU).
+Two exchange backends:
+
+* ``"p2p"`` (default, up to 8 ranks on one node): every rank shares one
+  region of its HBM with the others through CUDA IPC.  Counts go out with peer
+  stores and flags, senders write rows straight into the owners' expert-major
+  buffers and owners write results straight back into the sources' packed
+  slots (``moe_ep_p2p``).  No host synchronisation: the whole step can be
+  captured in a CUDA graph.  Waits on peers are bounded and report through
+  ``moe_device_status``.
+* ``"nccl"``: steps 3-4 and 8 as ``all_to_all_single`` with the split sizes
+  read on the host (one synchronisation per forward), and the regroup kernels.
+  The count, split and row-exchange helpers take any process group and tensors
+  on any device (the gloo tests run them on CPU).
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
@@ -81,6 +93,73 @@ class _Buffers:
         return t
 
 
+class _DeviceArray:
+    """A raw device allocation seen as an array (for torch.as_tensor, zero copy)."""
+
+    def __init__(self, address, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(address), False), "version": 3,
+                                         "strides": None}
+
+
+class PeerExchange:
+    """This rank's P2P exchange region (shared over CUDA IPC), the peers' regions
+    mapped into this process, and the rank-local step state."""
+
+    def __init__(self, lib, group, ranks, rank, experts, hidden, grouped_rows, back_rows,
+                 device):
+        self.lib, self.ranks, self.rank = lib, ranks, rank
+        self.shape = (experts, hidden, grouped_rows, back_rows)
+        nbytes = lib.moe_ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows)
+        if nbytes < 0:
+            raise ValueError("expert-parallel P2P needs <= 8 ranks, experts divisible by ranks")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        self._check(lib.moe_peer_alloc(nbytes, ctypes.addressof(own), ctypes.addressof(handle)))
+        self.own = own.value
+        handles = [None] * ranks
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.opened, bases = [], []
+        for r in range(ranks):
+            if r == rank:
+                bases.append(self.own)
+                continue
+            peer = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(handles[r])
+            self._check(lib.moe_peer_open(ctypes.addressof(buf), ctypes.addressof(peer)))
+            self.opened.append(peer.value)
+            bases.append(peer.value)
+        self.regions = (ctypes.c_void_p * ranks)(*bases)
+        words = lib.moe_ep_p2p_state_words(ranks, experts)
+        self.state = torch.zeros(words, dtype=torch.int32, device=device)
+        g_off = lib.moe_ep_p2p_region_offset(ranks, experts, hidden, grouped_rows, back_rows, 0)
+        b_off = lib.moe_ep_p2p_region_offset(ranks, experts, hidden, grouped_rows, back_rows, 1)
+        self.grouped = torch.as_tensor(
+            _DeviceArray(self.own + g_off, (grouped_rows, hidden), "<i2"), device=device
+        ).view(torch.bfloat16)
+        self.back = torch.as_tensor(
+            _DeviceArray(self.own + b_off, (back_rows, hidden), "<i2"), device=device
+        ).view(torch.bfloat16)
+        local = experts // ranks
+        self.offsets = self.state[4 + experts: 4 + experts + local + 1]
+        dist.barrier(group=group)
+
+    def _check(self, status):
+        if status != 0:
+            raise RuntimeError(self.lib.moe_last_error().decode())
+
+    def close(self):
+        """Unmap the peers' regions and free this rank's (after the device is idle)."""
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        self.grouped = self.back = None
+        for ptr in self.opened:
+            self.lib.moe_peer_close(ptr)
+        self.lib.moe_peer_free(self.own)
+        self.own, self.opened = None, []
+
+
 class ExpertParallelMoEBlock(torch.nn.Module):
     """MoE block whose experts are sharded over the ranks of `group`.
 
@@ -90,7 +169,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     """
 
     def __init__(self, config, router_weight, gate_up, down, *, group=None, device="cuda",
-                 routing_bias=None):
+                 routing_bias=None, backend=None, timeout_ms=10000):
         super().__init__()
         self.config = config if isinstance(config, MoEConfig) else MoEConfig(*config)
         self.group = group
@@ -116,6 +195,13 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self._route = {}
         self._rows = _Buffers()
         self.last_split_sizes = None
+        if backend is None:
+            backend = "p2p" if self.ranks <= 8 else "nccl"
+        if backend not in ("p2p", "nccl"):
+            raise ValueError("backend must be p2p or nccl")
+        self.backend = backend
+        self.timeout_ms = int(timeout_ms)
+        self.exchange = None
 
     def _state(self, x):
         key = (x.shape[0], x.device)
@@ -159,6 +245,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         if tokens:
             ext.route_out(x, self.router_weight, self.routing_bias, logits, ids32, ids64, weights)
         transport.dispatch(x, ids32, ids64)
+        if self.backend == "p2p":
+            return self._forward_p2p(x, transport, weights, mark)
         recv_counts = exchange_counts(transport.counts, self.ranks, self.group)
         send_rows, recv_rows = split_sizes(transport.counts, recv_counts, self.ranks)
         self.last_split_sizes = (send_rows, recv_rows)
@@ -189,3 +277,62 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         if tokens:
             transport.combine(back[:n], weights)
         return transport.output
+
+    def _peer_exchange(self, tokens, device):
+        cfg = self.config
+        grouped_rows = capacity_rows(self.ranks * tokens * min(cfg.topk, self.local_experts),
+                                     self.local_experts, 1, cfg.alignment)
+        back_rows = max(tokens * cfg.topk, 1)
+        if self.exchange is not None and self.exchange.shape == (cfg.experts, cfg.hidden,
+                                                                 grouped_rows, back_rows):
+            return self.exchange
+        if self.exchange is not None:
+            self.exchange.close()
+        self.exchange = PeerExchange(self.extension.lib, self.group, self.ranks, self.rank,
+                                     cfg.experts, cfg.hidden, grouped_rows, back_rows, device)
+        return self.exchange
+
+    def _p2p(self, op, rows, aux):
+        ex = self.exchange
+        experts, hidden, grouped_rows, back_rows = ex.shape
+        self.extension._call(
+            ex.state.device, self.extension.lib.moe_ep_p2p, op,
+            None if rows is None else rows.data_ptr(), None if aux is None else aux.data_ptr(),
+            ctypes.addressof(ex.regions), ex.state.data_ptr(), self.ranks, self.rank, experts,
+            self.config.alignment, hidden, grouped_rows, back_rows, self.timeout_ms,
+        )
+
+    def _forward_p2p(self, x, transport, weights, mark):
+        """Steps 3-8 over peer memory: no host synchronisation (graph-capturable)."""
+        cfg = self.config
+        ext = self.extension
+        tokens = x.shape[0]
+        n = tokens * cfg.topk
+        ex = self._peer_exchange(tokens, x.device)
+        rows = ex.grouped.shape[0]
+        activated = self._rows.get("activated", rows, cfg.intermediate, x.dtype, x.device)
+        expert_out = self._rows.get("expert_out", rows, cfg.hidden, x.dtype, x.device)
+        self._p2p(0, None, transport.counts)
+        mark("exchange", 0)
+        self._p2p(1, transport.packed, transport.offsets)
+        self._p2p(2, None, None)
+        mark("exchange", 1)
+        mark("gemm1", 0)
+        ext.grouped_gemm_swiglu_out(ex.grouped, self.gate_up_weight, ex.offsets, activated)
+        mark("gemm1", 1)
+        mark("gemm2", 0)
+        ext.grouped_gemm_out(activated, self.down_weight, ex.offsets, expert_out)
+        mark("gemm2", 1)
+        mark("return", 0)
+        self._p2p(3, expert_out, None)
+        self._p2p(4, None, None)
+        mark("return", 1)
+        if tokens:
+            transport.combine(ex.back[:n], weights)
+        return transport.output
+
+    def close(self):
+        """Release the P2P exchange region (call on every rank, before the process group ends)."""
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None

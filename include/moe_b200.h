@@ -168,6 +168,50 @@ int moe_ep_regroup(const void* from, int32_t dtype, void* to, const int32_t* cou
                    int32_t ranks, int32_t experts, int64_t hidden, int64_t recv_rows,
                    int64_t grouped_rows, int32_t grouping, void* stream);
 
+/* Peer memory for the NVLink exchange (new; the reference is single-GPU).
+ * moe_peer_alloc allocates `bytes` of zeroed device memory on the current
+ * device and writes its 64-byte CUDA IPC handle to `ipc_handle`; another
+ * process on the node maps it with moe_peer_open (and unmaps it with
+ * moe_peer_close).  moe_peer_free releases the allocation.  Set-up calls:
+ * they allocate and synchronise, so make them outside any timed or captured
+ * region. */
+int moe_peer_alloc(int64_t bytes, void** ptr, void* ipc_handle);
+int moe_peer_open(const void* ipc_handle, void** ptr);
+int moe_peer_close(void* ptr);
+int moe_peer_free(void* ptr);
+
+/* Layout of one rank's exchange region and local state for the P2P
+ * expert-parallel step (ranks <= 8, experts a multiple of ranks, bf16 rows of
+ * `hidden`): total bytes; byte offset of the grouped rows (section 0, capacity
+ * grouped_rows) or of the returned rows (section 1, capacity back_rows); and
+ * the int32 words of per-rank local state (zeroed once before the first step).
+ * -1 on invalid arguments. */
+int64_t moe_ep_p2p_region_bytes(int32_t ranks, int32_t experts, int64_t hidden,
+                                int64_t grouped_rows, int64_t back_rows);
+int64_t moe_ep_p2p_region_offset(int32_t ranks, int32_t experts, int64_t hidden,
+                                 int64_t grouped_rows, int64_t back_rows, int32_t section);
+int64_t moe_ep_p2p_state_words(int32_t ranks, int32_t experts);
+
+/* One stage of the P2P expert-parallel step, enqueued on `stream` (no host
+ * sync).  regions[P] are the ranks' exchange regions as mapped in this process
+ * (this rank's own at regions[rank]).  op:
+ *   0 exchange counts: aux = counts[E] from moe_dispatch; writes them to every
+ *     rank, waits for all ranks', computes the send/receive tables and this
+ *     rank's grouped expert offsets (state words 4+E .. 4+E+E_l);
+ *   1 send rows: rows = the compact packed rows, aux = moe_dispatch's offsets;
+ *     each row lands in its expert owner's grouped rows, source-major inside
+ *     an expert (the global token order); the last CTA raises the rows flags;
+ *   2 wait until every rank's rows arrived;
+ *   3 return rows: rows = this rank's expert outputs in grouped order; each
+ *     row goes back to its source's returned rows at its packed position;
+ *   4 wait until every rank's results came back.
+ * Waits give up after timeout_ms, record status 2 (read by
+ * moe_device_status) and return; capacity overflows record status 3. */
+int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* regions,
+               int32_t* state, int32_t ranks, int32_t rank, int32_t experts, int32_t alignment,
+               int64_t hidden, int64_t grouped_rows, int64_t back_rows, int64_t timeout_ms,
+               void* stream);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* Reads (and with clear != 0 resets) the current device's status word, which

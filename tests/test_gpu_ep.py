@@ -68,7 +68,8 @@ def _port():
         return s.getsockname()[1]
 
 
-def test_single_rank_expert_parallel_block_equals_moeblock():
+@pytest.mark.parametrize("backend", ["p2p", "nccl"])
+def test_single_rank_expert_parallel_block_equals_moeblock(backend):
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock
     from moe_dispatch.layer import MoEBlock, MoEConfig, MoEWeights
     from moe_dispatch.routing import BlockWorkload, block_input, block_weights
@@ -86,10 +87,46 @@ def test_single_rank_expert_parallel_block_equals_moeblock():
                                                   weights.down.cuda()))
         single.routing_bias.copy_(bias)
         ep = ExpertParallelMoEBlock(cfg, weights.router, weights.gate_up, weights.down,
-                                    routing_bias=bias)
+                                    routing_bias=bias, backend=backend)
         expected = single(x).clone()
         assert torch.equal(ep(x).clone(), expected)
         assert torch.equal(ep(x).clone(), expected)
+        assert ep.extension.device_status() == 0
+        ep.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_p2p_wait_gives_up_and_reports_instead_of_hanging():
+    """A flag nobody raises: the bounded wait must end, record status 2, and
+    leave the context usable (no trap, no hang)."""
+    import ctypes
+
+    from moe_dispatch.expert_parallel import PeerExchange
+
+    ext_ = __import__("moe_dispatch").get_extension()
+    if not dist.is_initialized():
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{_port()}", rank=0,
+                                world_size=1, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", 0))
+    try:
+        ex = PeerExchange(ext_.lib, None, 1, 0, 8, 64, 64, 16, torch.device("cuda", 0))
+        counts = torch.zeros(8, dtype=torch.int32, device="cuda")
+        ext_.device_status(clear=True)
+        stream = torch.cuda.current_stream().cuda_stream
+
+        def op(code, aux=None):
+            status = ext_.lib.moe_ep_p2p(code, None, None if aux is None else aux.data_ptr(),
+                                         ctypes.addressof(ex.regions), ex.state.data_ptr(), 1, 0,
+                                         8, 8, 64, 64, 16, 300, stream)
+            assert status == 0, ext_.lib.moe_last_error().decode()
+
+        op(0, counts)      # count exchange with itself: completes
+        op(2)              # rows flag never raised: must time out after 300 ms
+        torch.cuda.synchronize()
+        assert ext_.device_status(clear=True) == 2
+        assert torch.ones(4, device="cuda").sum().item() == 4.0  # context still usable
+        ex.close()
     finally:
         dist.destroy_process_group()
 
