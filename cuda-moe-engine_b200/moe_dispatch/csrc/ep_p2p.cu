@@ -120,6 +120,29 @@ __device__ bool wait_flags(const uint32_t* flags, int ranks, uint32_t epoch, uin
     return failed == 0;
 }
 
+// One warp copies one row: batches of 8 16-byte loads per lane are issued
+// before their stores, so each lane keeps 128 bytes in flight (peer stores over
+// NVLink need many outstanding requests to reach link bandwidth).
+__device__ __forceinline__ void warp_copy_row(uint4* __restrict__ target, const uint4* __restrict__ source,
+                                              int64_t row_vecs, int lane) {
+    constexpr int kBatch = 8;
+    for (int64_t c0 = lane; c0 < row_vecs; c0 += 32 * kBatch) {
+        uint4 v[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int64_t c = c0 + 32 * b;
+            if (c < row_vecs) v[b] = __ldg(source + c);
+        }
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b) {
+            const int64_t c = c0 + 32 * b;
+            if (c < row_vecs) target[c] = v[b];
+        }
+    }
+}
+
+constexpr int kCopyThreads = 256;
+
 __global__ void __launch_bounds__(1024)
 ep_exchange_counts_kernel(const int32_t* __restrict__ counts, Regions regions, int32_t* state_base,
                           int ranks, int me, int experts, int alignment, int64_t hidden,
@@ -193,8 +216,8 @@ ep_exchange_counts_kernel(const int32_t* __restrict__ counts, Regions regions, i
     if (tid == 0) *st.epoch = static_cast<int32_t>(epoch);
 }
 
-// Rows of my compact packed buffer -> their owners' grouped buffers.
-__global__ void __launch_bounds__(128)
+// Rows of my compact packed buffer -> their owners' grouped buffers (a warp per row).
+__global__ void __launch_bounds__(kCopyThreads)
 ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict__ dispatch_offsets,
                     Regions regions, int32_t* state_base, int ranks, int me, int experts,
                     int64_t row_vecs, int64_t hidden, int64_t grouped_rows, int64_t back_rows) {
@@ -202,7 +225,10 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
     State st = state_view(state_base, ranks, experts);
     const int local = experts / ranks;
     const int64_t rows = dispatch_offsets[experts];
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; r < rows;
+         r += warps) {
         int lo = 0, hi = experts - 1;  // expert of packed row r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -212,12 +238,11 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
         const int owner = lo / local;
         const int64_t dst = st.send_dst[lo] + (r - dispatch_offsets[lo]);
         if (dst >= grouped_rows) {
-            if (threadIdx.x == 0) atomicCAS(&g_ep_status, 0, 3);
+            if (lane == 0) atomicCAS(&g_ep_status, 0, 3);
             continue;
         }
         uint4* target = reinterpret_cast<uint4*>(regions.base[owner] + l.grouped) + dst * row_vecs;
-        const uint4* source = packed + r * row_vecs;
-        for (int64_t c = threadIdx.x; c < row_vecs; c += blockDim.x) target[c] = source[c];
+        warp_copy_row(target, packed + r * row_vecs, row_vecs, lane);
     }
     // the last CTA to finish raises the rows flag of source `me` on every rank
     __threadfence_system();
@@ -234,8 +259,8 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
     if (threadIdx.x == 0) st.counters[0] = 0;
 }
 
-// Result rows of my grouped buffer -> the `back` buffers of their sources.
-__global__ void __launch_bounds__(128)
+// Result rows of my grouped buffer -> the `back` buffers of their sources (a warp per row).
+__global__ void __launch_bounds__(kCopyThreads)
 ep_return_rows_kernel(const uint4* __restrict__ results, Regions regions, int32_t* state_base,
                       int ranks, int me, int experts, int64_t row_vecs, int64_t hidden,
                       int64_t grouped_rows, int64_t back_rows) {
@@ -244,7 +269,10 @@ ep_return_rows_kernel(const uint4* __restrict__ results, Regions regions, int32_
     const int local = experts / ranks;
     const int segments = ranks * local;
     const int64_t rows = st.recv_prefix[segments];
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
+    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; r < rows;
+         r += warps) {
         int lo = 0, hi = segments - 1;  // last segment starting at or before r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -256,12 +284,11 @@ ep_return_rows_kernel(const uint4* __restrict__ results, Regions regions, int32_
         const int source = lo / local;
         const int64_t dst = st.ret_dst[lo] + i;
         if (dst >= back_rows) {
-            if (threadIdx.x == 0) atomicCAS(&g_ep_status, 0, 3);
+            if (lane == 0) atomicCAS(&g_ep_status, 0, 3);
             continue;
         }
         uint4* target = reinterpret_cast<uint4*>(regions.base[source] + l.back) + dst * row_vecs;
-        const uint4* from = results + (st.seg_start[lo] + i) * row_vecs;
-        for (int64_t c = threadIdx.x; c < row_vecs; c += blockDim.x) target[c] = from[c];
+        warp_copy_row(target, results + (st.seg_start[lo] + i) * row_vecs, row_vecs, lane);
     }
     __threadfence_system();
     __syncthreads();
@@ -327,12 +354,12 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
             break;
         }
         case kEpP2pSend:
-            ep_send_rows_kernel<<<148 * 8, 128, 0, stream>>>(static_cast<const uint4*>(rows), aux, r,
+            ep_send_rows_kernel<<<148 * 4, kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), aux, r,
                                                              state, ranks, me, experts, row_vecs,
                                                              hidden, grouped_rows, back_rows);
             break;
         case kEpP2pReturn:
-            ep_return_rows_kernel<<<148 * 8, 128, 0, stream>>>(static_cast<const uint4*>(rows), r,
+            ep_return_rows_kernel<<<148 * 4, kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), r,
                                                                state, ranks, me, experts, row_vecs,
                                                                hidden, grouped_rows, back_rows);
             break;

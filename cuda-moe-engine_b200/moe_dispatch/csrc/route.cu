@@ -22,23 +22,65 @@
 namespace moe {
 namespace {
 
-constexpr int kRouteChunk = 32;  // hidden elements staged per step
-
-// Tiled SIMT GEMM: a CTA owns TT tokens x TE experts; each thread owns MT x ME
-// logits.  Every logit accumulates in h order, so tiling does not change its value.
-template <int TT, int TE, int MT, int ME>
-__global__ void __launch_bounds__((TT / MT) * (TE / ME))
-router_logits_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
-                     float* __restrict__ logits, int64_t tokens, int hidden, int experts) {
-    constexpr int kThreads = (TT / MT) * (TE / ME);
-    constexpr int kTx = TE / ME;
-    __shared__ float xs[kRouteChunk][TT + 4];
-    __shared__ __align__(16) float ws[kRouteChunk][TE + 4];
-
+// Many experts (E > 32): 128-token x TE-expert tiles, 256 threads, an MT x ME
+// register micro-tile per thread, hidden consumed in chunks of 16 staged in
+// two shared-memory buffers (the next chunk's global loads are in flight while
+// the current one is used).  Every logit is still one sequential FMA chain in
+// increasing h, so the tiling does not change any value.
+template <int TE, int ME>
+__global__ void __launch_bounds__(256)
+router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                           float* __restrict__ logits, int64_t tokens, int hidden, int experts) {
+    constexpr int TT = 128, MT = 8, KC = 16;
+    constexpr int kTx = TE / ME;  // threads along experts
+    static_assert((TT / MT) * kTx == 256, "256 threads");
+    __shared__ __align__(16) float xs[2][KC][TT];
+    __shared__ __align__(16) float ws[2][KC][TE];
     const int tid = threadIdx.x;
     const int tx = tid % kTx, ty = tid / kTx;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
     const int e0 = blockIdx.y * TE;
+
+    // global -> register staging: x 128 rows x 16 h (bf16) = one 16-byte piece per
+    // thread; W TE rows x 16 h (fp32) = TE*4 16-byte pieces.
+    constexpr int kWPieces = TE * KC / 4 / 256;
+    uint4 xr;
+    float4 wr[kWPieces];
+    auto load = [&](int h0) {
+        const int row = tid >> 1, half = tid & 1;
+        const int64_t t = t0 + row;
+        const int h = h0 + half * 8;
+        xr = make_uint4(0, 0, 0, 0);
+        if (t < tokens && h < hidden) xr = __ldg(reinterpret_cast<const uint4*>(x + t * hidden + h));
+#pragma unroll
+        for (int q = 0; q < kWPieces; ++q) {
+            const int v = tid + q * 256;
+            const int er = v >> 2, piece = v & 3;
+            const int e = e0 + er;
+            const int hh = h0 + piece * 4;
+            wr[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e < experts && hh < hidden)
+                wr[q] = __ldg(reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + hh));
+        }
+    };
+    auto store = [&](int buf) {
+        const int row = tid >> 1, half = tid & 1;
+        const uint32_t words[4] = {xr.x, xr.y, xr.z, xr.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xs[buf][half * 8 + 2 * q][row] = bf16_bits_to_f32(words[q] & 0xffffu);
+            xs[buf][half * 8 + 2 * q + 1][row] = bf16_bits_to_f32(words[q] >> 16);
+        }
+#pragma unroll
+        for (int q = 0; q < kWPieces; ++q) {
+            const int v = tid + q * 256;
+            const int er = v >> 2, piece = v & 3;
+            ws[buf][piece * 4 + 0][er] = wr[q].x;
+            ws[buf][piece * 4 + 1][er] = wr[q].y;
+            ws[buf][piece * 4 + 2][er] = wr[q].z;
+            ws[buf][piece * 4 + 3][er] = wr[q].w;
+        }
+    };
 
     float acc[MT][ME];
 #pragma unroll
@@ -46,49 +88,33 @@ router_logits_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
 #pragma unroll
         for (int j = 0; j < ME; ++j) acc[i][j] = 0.0f;
 
-    for (int h0 = 0; h0 < hidden; h0 += kRouteChunk) {
-        // x tile: TT rows x 32 columns, four 16-byte pieces per row.
-        for (int v = tid; v < TT * 4; v += kThreads) {
-            const int row = v >> 2, piece = v & 3;
-            const int64_t t = t0 + row;
-            const int h = h0 + piece * 8;
-            uint4 raw = make_uint4(0, 0, 0, 0);
-            if (t < tokens && h < hidden)
-                raw = __ldg(reinterpret_cast<const uint4*>(x + t * hidden + h));
-            const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                xs[piece * 8 + 2 * q][row] = bf16_bits_to_f32(words[q] & 0xffffu);
-                xs[piece * 8 + 2 * q + 1][row] = bf16_bits_to_f32(words[q] >> 16);
-            }
-        }
-        // W tile: TE rows x 32 columns of fp32, eight 16-byte pieces per row.
-        for (int v = tid; v < TE * 8; v += kThreads) {
-            const int row = v >> 3, piece = v & 7;
-            const int e = e0 + row;
-            const int h = h0 + piece * 4;
-            float4 val = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < experts && h < hidden)
-                val = __ldg(reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + h));
-            ws[piece * 4 + 0][row] = val.x;
-            ws[piece * 4 + 1][row] = val.y;
-            ws[piece * 4 + 2][row] = val.z;
-            ws[piece * 4 + 3][row] = val.w;
-        }
+    load(0);
+    int buf = 0;
+    for (int h0 = 0; h0 < hidden; h0 += KC) {
+        store(buf);
         __syncthreads();
-        const int steps = min(kRouteChunk, hidden - h0);
-        for (int kk = 0; kk < steps; ++kk) {
+        if (h0 + KC < hidden) load(h0 + KC);
+        const int steps = min(KC, hidden - h0);
+        for (int k = 0; k < steps; ++k) {
             float xv[MT], wv[ME];
+            const float4* xp = reinterpret_cast<const float4*>(&xs[buf][k][ty * MT]);
+            const float4* wp = reinterpret_cast<const float4*>(&ws[buf][k][tx * ME]);
 #pragma unroll
-            for (int i = 0; i < MT; ++i) xv[i] = xs[kk][ty * MT + i];
+            for (int q = 0; q < MT / 4; ++q) {
+                const float4 v = xp[q];
+                xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
+            }
 #pragma unroll
-            for (int j = 0; j < ME; ++j) wv[j] = ws[kk][tx * ME + j];
+            for (int q = 0; q < ME / 4; ++q) {
+                const float4 v = wp[q];
+                wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+            }
 #pragma unroll
             for (int i = 0; i < MT; ++i)
 #pragma unroll
                 for (int j = 0; j < ME; ++j) acc[i][j] = fmaf(xv[i], wv[j], acc[i][j]);
         }
-        __syncthreads();
+        buf ^= 1;
     }
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
@@ -280,10 +306,17 @@ topk_softmax_kernel(const float* __restrict__ logits, const float* __restrict__ 
 cudaError_t launch_router_logits(const void* x, const float* w, float* logits, int64_t tokens,
                                  int64_t hidden, int experts, cudaStream_t stream) {
     if (tokens == 0) return cudaSuccess;
-    constexpr int TT = 64, TE = 64;
-    dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), (experts + TE - 1) / TE);
-    router_logits_kernel<TT, TE, 4, 4><<<grid, (TT / 4) * (TE / 4), 0, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), w, logits, tokens, static_cast<int>(hidden), experts);
+    const auto* xb = static_cast<const __nv_bfloat16*>(x);
+    const unsigned token_tiles = static_cast<unsigned>((tokens + 127) / 128);
+    if (experts <= 64) {
+        dim3 grid(token_tiles, (experts + 63) / 64);
+        router_logits_tiled_kernel<64, 4><<<grid, 256, 0, stream>>>(xb, w, logits, tokens,
+                                                                    static_cast<int>(hidden), experts);
+    } else {
+        dim3 grid(token_tiles, (experts + 127) / 128);
+        router_logits_tiled_kernel<128, 8><<<grid, 256, 0, stream>>>(xb, w, logits, tokens,
+                                                                     static_cast<int>(hidden), experts);
+    }
     return cudaGetLastError();
 }
 
