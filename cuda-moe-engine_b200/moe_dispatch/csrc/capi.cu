@@ -335,6 +335,30 @@ int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* re
                        "moe_ep_p2p");
 }
 
+int moe_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,
+                           int32_t* state, int32_t ranks, int32_t rank, int32_t experts,
+                           int64_t hidden, int64_t intermediate, int64_t grouped_rows,
+                           int64_t back_rows, void* stream) {
+    if (moe_ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows) < 0)
+        return fail(MOE_ERR_INVALID, "expert-parallel P2P: 1 <= ranks <= %d, experts a multiple "
+                                     "of ranks, hidden a multiple of 8", moe::kEpP2pMaxRanks);
+    if (rank < 0 || rank >= ranks) return fail(MOE_ERR_INVALID, "rank out of range");
+    if (intermediate < 8 || intermediate % 8 || grouped_rows < 1 || grouped_rows > INT_MAX)
+        return fail(MOE_ERR_INVALID, "invalid down GEMM shape");
+    if (!activated || !down || !regions || !state || !aligned(activated, 16) || !aligned(down, 16))
+        return fail(MOE_ERR_INVALID, "null or unaligned pointer");
+    for (int i = 0; i < ranks; ++i)
+        if (!regions[i] || !aligned(regions[i], 1024))
+            return fail(MOE_ERR_INVALID, "peer regions must be non-null and 1024-byte aligned");
+    const char* message = nullptr;
+    cudaError_t err = moe::launch_ep_p2p_down_return(activated, down, regions, state, ranks, rank,
+                                                     experts, hidden, intermediate, grouped_rows,
+                                                     back_rows, static_cast<cudaStream_t>(stream),
+                                                     &message);
+    if (message) return fail(MOE_ERR_INVALID, "%s", message);
+    return cuda_status(err, "moe_ep_p2p_down_return");
+}
+
 int moe_device_status(int32_t* code, int32_t clear) {
     if (!code) return fail(MOE_ERR_INVALID, "code must be non-null");
     int32_t gemm = 0, ep = 0;

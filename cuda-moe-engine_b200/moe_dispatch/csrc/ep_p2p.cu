@@ -375,6 +375,29 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
     return cudaGetLastError();
 }
 
+cudaError_t launch_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,
+                                      int32_t* state, int ranks, int me, int experts,
+                                      int64_t hidden, int64_t intermediate, int64_t grouped_rows,
+                                      int64_t back_rows, cudaStream_t stream, const char** error) {
+    const Layout l = region_layout(ranks, experts, hidden, grouped_rows, back_rows);
+    const State st = state_view(state, ranks, experts);
+    GemmScatter sc = {};
+    for (int i = 0; i < ranks; ++i) sc.base[i] = static_cast<char*>(regions[i]);
+    sc.back_offset = l.back;
+    sc.flags_offset = l.flags;
+    sc.back_rows = back_rows;
+    sc.seg_start = st.seg_start;
+    sc.seg_count = st.seg_count;
+    sc.ret_dst = st.ret_dst;
+    sc.epoch = st.epoch;
+    sc.ticket = st.counters + 1;
+    sc.ranks = ranks;
+    sc.me = me;
+    sc.local_experts = experts / ranks;
+    return launch_grouped_gemm_scatter(activated, down, st.offsets, grouped_rows, hidden,
+                                       intermediate, experts / ranks, sc, stream, error);
+}
+
 cudaError_t read_ep_status(int32_t* code, bool clear) {
     MOE_CUDA_TRY(cudaMemcpyFromSymbol(code, g_ep_status, sizeof(int32_t)));
     if (clear) {

@@ -218,10 +218,12 @@ __device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int exp
     m = local - n * mt;
 }
 
-template <bool kSwiglu>
+template <bool kSwiglu, bool kScatter = false>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                    const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmap_b, const GemmParams p,
+                    const GemmScatter scatter) {
+    static_assert(!(kSwiglu && kScatter), "the scatter epilogue is for the down GEMM");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -385,9 +387,25 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
             tc_fence_after();
             const int64_t row = static_cast<int64_t>(p.offsets[e]) + m * kBM + quarter * 32 + lane;
-            const bool valid = row < p.offsets[e + 1];
+            bool valid = row < p.offsets[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
+            if constexpr (kScatter) {
+                // the source rank and packed row this grouped row returns to
+                valid = false;
+                for (int src = 0; src < scatter.ranks; ++src) {
+                    const int seg = src * scatter.local_experts + e;
+                    const int64_t start = scatter.seg_start[seg];
+                    if (row >= start && row < start + scatter.seg_count[seg]) {
+                        const int64_t back = scatter.ret_dst[seg] + (row - start);
+                        if (back < scatter.back_rows) {
+                            valid = true;
+                            dst_row = reinterpret_cast<__nv_bfloat16*>(
+                                          scatter.base[src] + scatter.back_offset) + back * p.ldo;
+                        }
+                    }
+                }
+            }
 #pragma unroll 1
             for (int c = 0; c < kOutTile; c += 32) {
                 uint32_t v[32];
@@ -428,6 +446,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             tc_fence_before();
             mbar_arrive(&tmem_empty[acc]);
         }
+        if constexpr (kScatter) __threadfence_system();  // results visible on their ranks
     }
 
     tc_fence_before();
@@ -436,6 +455,22 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(kTmemCols));
+    }
+    if constexpr (kScatter) {
+        // the last CTA to finish raises this rank's return flag on every rank
+        if (threadIdx.x == 0) {
+            __threadfence_system();
+            if (atomicAdd(scatter.ticket, 1) == static_cast<int>(gridDim.x) - 1) {
+                __threadfence_system();
+                const uint32_t epoch = static_cast<uint32_t>(*scatter.epoch);
+                for (int r = 0; r < scatter.ranks; ++r) {
+                    uint32_t* flag = reinterpret_cast<uint32_t*>(scatter.base[r] + scatter.flags_offset) +
+                                     2 * kGemmScatterMaxRanks + scatter.me;
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+                }
+                *scatter.ticket = 0;
+            }
+        }
     }
 }
 
@@ -871,7 +906,49 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     }
     const int64_t max_tiles = ((rows + kBM - 1) / kBM + experts) * static_cast<int64_t>(p.n_tiles);
     const int grid = static_cast<int>(max_tiles < info.sms ? max_tiles : info.sms);
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p);
+    const GemmScatter none = {};
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, none);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int32_t* offsets,
+                                        int64_t rows, int64_t n_out, int64_t k_dim, int experts,
+                                        const GemmScatter& scatter, cudaStream_t stream,
+                                        const char** error) {
+    *error = nullptr;
+    if (experts > kMaxExperts) {
+        *error = "grouped GEMM supports at most 1024 experts";
+        return cudaErrorInvalidValue;
+    }
+    int device = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&device));
+    DeviceInfo& info = device_info(device);
+    if (info.sms == 0) MOE_CUDA_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
+    static bool configured[64] = {};
+    auto kernel = grouped_gemm_kernel<false, true>;
+    if (!configured[device & 63]) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+        configured[device & 63] = true;
+    }
+    CUtensorMap map_a, map_b;
+    const uint64_t a_rows = static_cast<uint64_t>(rows > 0 ? rows : 1);
+    if (!make_tensor_map(&map_a, a, a_rows, static_cast<uint64_t>(k_dim)) ||
+        !make_tensor_map(&map_b, b, static_cast<uint64_t>(n_out * experts), static_cast<uint64_t>(k_dim))) {
+        *error = "cuTensorMapEncodeTiled rejected an operand (pointer alignment or shape)";
+        return cudaErrorInvalidValue;
+    }
+    GemmParams p;
+    p.offsets = offsets;
+    p.out = nullptr;
+    p.ldo = n_out;
+    p.n_out = static_cast<int>(n_out);
+    p.k_dim = static_cast<int>(k_dim);
+    p.experts = experts;
+    p.n_tiles = static_cast<int>((n_out + kBN - 1) / kBN);
+    p.b_rows = static_cast<int>(n_out);
+    p.up_offset = 0;
+    // every CTA takes part in the completion ticket, so the grid never depends on the rows
+    kernel<<<info.sms, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, scatter);
     return cudaGetLastError();
 }
 

@@ -42,6 +42,27 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
                                 bool swiglu, cudaStream_t stream, const char** error);
 cudaError_t read_gemm_status(int32_t* code, bool clear);
 
+// Down GEMM whose epilogue returns each result row to its source rank (P2P
+// expert parallelism): grouped row r of local expert e belongs to the segment
+// s with seg_start[s*E_l+e] <= r < seg_start + seg_count; it is stored at row
+// ret_dst[s*E_l+e] + (r - seg_start) of rank s's `back` section.  After the
+// last CTA finishes, return flag `me` is raised on every rank with *epoch.
+constexpr int kGemmScatterMaxRanks = 8;
+struct GemmScatter {
+    char* base[kGemmScatterMaxRanks];
+    int64_t back_offset, flags_offset, back_rows;
+    const int32_t* seg_start;
+    const int32_t* seg_count;
+    const int32_t* ret_dst;
+    const int32_t* epoch;
+    int32_t* ticket;
+    int ranks, me, local_experts;
+};
+cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int32_t* offsets,
+                                        int64_t rows, int64_t n_out, int64_t k_dim, int experts,
+                                        const GemmScatter& scatter, cudaStream_t stream,
+                                        const char** error);
+
 // Expert-parallel receive layout (ep.cu).
 cudaError_t launch_ep_layout(const int32_t* counts, int ranks, int experts, int alignment,
                              int32_t* src_start, int32_t* dst_start, int32_t* offsets,
@@ -66,6 +87,10 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
                           int64_t hidden, int64_t grouped_rows, int64_t back_rows,
                           int64_t timeout_ms, cudaStream_t stream);
 cudaError_t read_ep_status(int32_t* code, bool clear);
+cudaError_t launch_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,
+                                      int32_t* state, int ranks, int me, int experts,
+                                      int64_t hidden, int64_t intermediate, int64_t grouped_rows,
+                                      int64_t back_rows, cudaStream_t stream, const char** error);
 
 // Sets the calling thread's message returned by moe_last_error().
 void set_last_error(const char* message);

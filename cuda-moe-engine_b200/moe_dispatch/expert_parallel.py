@@ -166,10 +166,16 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     router_weight [E, H] fp32 and routing_bias [E] are replicated; gate_up
     [E_l, 2I, H] and down [E_l, H, I] are this rank's experts.  forward(x) takes
     this rank's tokens x [T_l, H] bf16 and returns their outputs [T_l, H].
+
+    fused_return=True (p2p only) runs the down GEMM with an epilogue that
+    stores each result row straight into its source rank's slot
+    (moe_ep_p2p_down_return) instead of a separate return copy.  Its stores go
+    out one row per lane; at the expert-parallel configuration the separate,
+    coalesced copy is faster, so it is off by default.
     """
 
     def __init__(self, config, router_weight, gate_up, down, *, group=None, device="cuda",
-                 routing_bias=None, backend=None, timeout_ms=10000):
+                 routing_bias=None, backend=None, timeout_ms=10000, fused_return=False):
         super().__init__()
         self.config = config if isinstance(config, MoEConfig) else MoEConfig(*config)
         self.group = group
@@ -201,6 +207,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             raise ValueError("backend must be p2p or nccl")
         self.backend = backend
         self.timeout_ms = int(timeout_ms)
+        self.fused_return = bool(fused_return)
         self.exchange = None
 
     def _state(self, x):
@@ -321,10 +328,20 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         ext.grouped_gemm_swiglu_out(ex.grouped, self.gate_up_weight, ex.offsets, activated)
         mark("gemm1", 1)
         mark("gemm2", 0)
-        ext.grouped_gemm_out(activated, self.down_weight, ex.offsets, expert_out)
-        mark("gemm2", 1)
-        mark("return", 0)
-        self._p2p(3, expert_out, None)
+        if self.fused_return:
+            # down GEMM whose epilogue writes each result row into its source's slot
+            experts, hidden, grouped_rows, back_rows = ex.shape
+            ext._call(ex.state.device, ext.lib.moe_ep_p2p_down_return, activated.data_ptr(),
+                      self.down_weight.data_ptr(), ctypes.addressof(ex.regions),
+                      ex.state.data_ptr(), self.ranks, self.rank, experts, hidden,
+                      cfg.intermediate, grouped_rows, back_rows)
+            mark("gemm2", 1)
+            mark("return", 0)
+        else:
+            ext.grouped_gemm_out(activated, self.down_weight, ex.offsets, expert_out)
+            mark("gemm2", 1)
+            mark("return", 0)
+            self._p2p(3, expert_out, None)
         self._p2p(4, None, None)
         mark("return", 1)
         if tokens:

@@ -212,6 +212,17 @@ int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* re
                int64_t hidden, int64_t grouped_rows, int64_t back_rows, int64_t timeout_ms,
                void* stream);
 
+/* The down GEMM of the P2P expert-parallel step fused with the return
+ * exchange (replaces moe_grouped_gemm + op 3 of moe_ep_p2p): tcgen05 grouped
+ * GEMM of activated [grouped_rows, intermediate] with this rank's down
+ * weights [E_l, hidden, intermediate]; its epilogue stores every result row
+ * straight into its source rank's returned rows at the packed position, and
+ * the last CTA raises the return flags.  Follow it with op 4 (wait). */
+int moe_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,
+                           int32_t* state, int32_t ranks, int32_t rank, int32_t experts,
+                           int64_t hidden, int64_t intermediate, int64_t grouped_rows,
+                           int64_t back_rows, void* stream);
+
 /* ------------------------------------------------------------ diagnostics */
 
 /* Reads (and with clear != 0 resets) the current device's status word, which

@@ -68,8 +68,8 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("backend", ["p2p", "nccl"])
-def test_single_rank_expert_parallel_block_equals_moeblock(backend):
+@pytest.mark.parametrize("backend,fused_return", [("p2p", True), ("p2p", False), ("nccl", False)])
+def test_single_rank_expert_parallel_block_equals_moeblock(backend, fused_return):
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock
     from moe_dispatch.layer import MoEBlock, MoEConfig, MoEWeights
     from moe_dispatch.routing import BlockWorkload, block_input, block_weights
@@ -87,7 +87,8 @@ def test_single_rank_expert_parallel_block_equals_moeblock(backend):
                                                   weights.down.cuda()))
         single.routing_bias.copy_(bias)
         ep = ExpertParallelMoEBlock(cfg, weights.router, weights.gate_up, weights.down,
-                                    routing_bias=bias, backend=backend)
+                                    routing_bias=bias, backend=backend,
+                                    fused_return=fused_return)
         expected = single(x).clone()
         assert torch.equal(ep(x).clone(), expected)
         assert torch.equal(ep(x).clone(), expected)
