@@ -116,9 +116,8 @@ __device__ __forceinline__ void record_status(int32_t code) { atomicCAS(&g_gemm_
 
 // Bounded wait for the phase of `bar` with the given parity.  Returns false
 // when the CTA is aborting (another role gave up) or this wait ran out.
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                       uint64_t limit_ns) {
-    if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity,
+                                            volatile int* abort_flag, uint64_t limit_ns) {
     const uint64_t start = global_timer();
     for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -131,6 +130,11 @@ __device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile 
             }
         }
     }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t limit_ns) {
+    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, limit_ns);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
@@ -824,14 +828,19 @@ DeviceInfo& device_info(int device) {
     return infos[device & 63];
 }
 
-// Tile shape selection: MOE_B200_GEMM_TILE=pair selects the CTA-pair kernel.
-// The default is the one-CTA tile: measured on B200 it is as fast or faster
-// for every block shape of the benchmark set except the fine-grained down
-// GEMM (6 % slower there), because the 256-row pair tile wastes more rows on
-// experts whose row count sits just above a multiple of the tile height.
-bool use_pair_tile(int64_t, int) {
+// Tile shape selection (MOE_B200_GEMM_TILE=pair|single overrides).  Measured on
+// B200, the 256-row CTA-pair tile wins the plain (down) GEMM once experts hold
+// about 512 rows or more on average (Mixtral 1024 rows/expert: 0.71 vs 0.79 ms;
+// 64 experts x 1536 rows: 0.46 vs 0.52 ms; 256 experts x 1024 rows: 7.13 vs
+// 7.52 ms), because it streams half the weight bytes per output row.  With
+// fewer rows per expert (256 experts x 256 rows: 2.94 vs 2.47 ms) and on the
+// SwiGLU GEMM, whose epilogue halves the tile's output width, the rows it pads
+// above each expert's last multiple of 256 cost more than that saves.
+bool use_pair_tile(int64_t rows, int experts, bool swiglu) {
     const char* env = getenv("MOE_B200_GEMM_TILE");
-    return env && env[0] == 'p';
+    if (env && env[0] == 'p') return true;
+    if (env && env[0] == 's') return false;
+    return !swiglu && rows >= 512 * static_cast<int64_t>(experts);
 }
 
 }  // namespace
@@ -868,7 +877,7 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     p.b_rows = static_cast<int>(b_rows);
     p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
 
-    if (use_pair_tile(rows, experts)) {
+    if (use_pair_tile(rows, experts, swiglu)) {
         auto kernel = swiglu ? grouped_gemm_pair_kernel<true> : grouped_gemm_pair_kernel<false>;
         cudaLaunchConfig_t config = {};
         cudaLaunchAttribute attribute[1];
