@@ -11,8 +11,11 @@ dispatch, gate/up GEMM with fused SwiGLU, down GEMM, combine.
   value      whole-job tokens/s with inputs resident in HBM: K replays of a
              CUDA graph of one step, CUDA events on the launching stream,
              barrier + synchronize on both sides, max over ranks.
-  e2e        the same metric through MoEBlock.__call__ with the step's x copied
-             from pinned host memory and the output copied back, every step.
+  e2e        the same metric through the public host-buffer API
+             (moe_dispatch.HostPipeline): every step copies its batch from
+             pinned host memory to the GPU, runs block(x, out=y) and copies y
+             back to pinned host memory; the copies run on two copy streams
+             and overlap the neighbouring steps' compute.
   roofline   the gate/up+SwiGLU GEMM (the dominant kernel): algorithmic FLOPs
              per launch / its mean CUDA-event duration over K eager steps.
   cpu_baseline  the CPU oracle (a C restatement of the reference's path) on a
@@ -21,8 +24,9 @@ dispatch, gate/up GEMM with fused SwiGLU, down GEMM, combine.
 With N > 1 (torchrun, one process per GPU) the block runs expert-parallel:
 the E experts are sharded evenly over the N ranks (rank r owns E/N of them),
 each rank routes its own T tokens (weak scaling), and token rows travel to
-their experts' ranks and back with NCCL all-to-all (ExpertParallelMoEBlock,
-eager: the split sizes need one host sync per step).
+their experts' ranks and back over NVLink peer memory (ExpertParallelMoEBlock,
+backend "p2p": no host sync, so the step is replayed as a CUDA graph;
+`--ep-backend nccl` uses NCCL all-to-all instead, eager, one host sync per step).
 `--impl reference` times the CPU port of the reference's path instead (rank 0
 only; the other ranks exit without work).
 """
@@ -233,6 +237,28 @@ def build_ep_block(workload, device, rank, world, backend=None):
     return block, x
 
 
+def time_host_pipeline(block, x, steps, world, device):
+    """Per-step ms of K batches through HostPipeline (pinned host in and out)."""
+    from moe_dispatch.host_pipeline import HostPipeline
+
+    pipe = HostPipeline(block, x.shape[0], device=device)
+    hosts = [x.cpu().pin_memory(), (x.cpu() * -1).pin_memory()]
+    outs = [torch.empty_like(hosts[0]).pin_memory() for _ in hosts]
+    pipe.run(hosts, outs)  # warm-up: fills both slots once
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(stream)
+    pipe.run([hosts[i % 2] for i in range(steps)], [outs[i % 2] for i in range(steps)],
+             synchronize=False)
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    h2d, d2h = pipe.bytes_per_batch()
+    return max_over_ranks(start.elapsed_time(end), world, device) / steps, h2d, d2h
+
+
 def run_expert_parallel(args, rank, world, local):
     from moe_dispatch.routing import WORKLOADS
 
@@ -288,23 +314,7 @@ def run_expert_parallel(args, rank, world, local):
         if block.backend == "nccl":
             send_rows, recv_rows = block.last_split_sizes
 
-        x_host = x.cpu().pin_memory()
-        out_host = torch.empty_like(x_host).pin_memory()
-        x_dev = torch.empty_like(x)
-        for _ in range(2):
-            x_dev.copy_(x_host, non_blocking=True)
-            out_host.copy_(block(x_dev), non_blocking=True)
-        e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize()
-        e2e_start.record(stream)
-        for _ in range(args.steps):
-            x_dev.copy_(x_host, non_blocking=True)
-            out_host.copy_(block(x_dev), non_blocking=True)
-        e2e_end.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device) / args.steps
+        e2e_ms, h2d_bytes, d2h_bytes = time_host_pipeline(block, x, args.steps, world, device)
         status = block.extension.device_status()
 
     hbm_peak, tf_peak, _, peak_kind = measured_peaks()
@@ -357,8 +367,10 @@ def run_expert_parallel(args, rank, world, local):
         "e2e": {
             "value": round(tokens * world / (e2e_ms / 1e3), 1),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-            "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+            "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": d2h_bytes,
+            "path": "HostPipeline.run: pinned host batch in, block(x, out=y), result out; "
+                    "copies on two copy streams overlap the neighbouring steps' compute",
         },
         "gpu_launches": (kernels_per_step(workload.experts) + (5 if graphed else 3)) * args.steps,
         "clocks": clocks.summary(),
@@ -423,23 +435,7 @@ def run_ours(args, rank, world, local):
         eager_ms = max_over_ranks(eager_start.elapsed_time(eager_end), world, device) / args.steps
 
         # -- end to end through the public API with host buffers
-        x_host = x.cpu().pin_memory()
-        out_host = torch.empty_like(x_host).pin_memory()
-        x_dev = torch.empty_like(x)
-        for _ in range(2):
-            x_dev.copy_(x_host, non_blocking=True)
-            out_host.copy_(block(x_dev), non_blocking=True)
-        e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier(world)
-        torch.cuda.synchronize()
-        e2e_start.record(stream)
-        for _ in range(args.steps):
-            x_dev.copy_(x_host, non_blocking=True)
-            out_host.copy_(block(x_dev), non_blocking=True)
-        e2e_end.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end), world, device) / args.steps
+        e2e_ms, h2d_bytes, d2h_bytes = time_host_pipeline(block, x, args.steps, world, device)
         status = block.extension.device_status()
 
     hbm_peak, tf_peak, tf_sustained, peak_kind = measured_peaks()
@@ -497,8 +493,10 @@ def run_ours(args, rank, world, local):
         "e2e": {
             "value": round(tokens * world / (e2e_ms / 1e3), 1),
             "unit": "tokens/s",
-            "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
-            "d2h_bytes_per_step": out_host.numel() * out_host.element_size(),
+            "h2d_bytes_per_step": h2d_bytes,
+            "d2h_bytes_per_step": d2h_bytes,
+            "path": "HostPipeline.run: pinned host batch in, block(x, out=y), result out; "
+                    "copies on two copy streams overlap the neighbouring steps' compute",
         },
         "gpu_launches": kernels_per_step(workload.experts) * args.steps,
         "clocks": clocks.summary(),

@@ -8,7 +8,7 @@ from importlib import import_module
 
 __version__ = "0.2.0+b200"
 __all__ = ["dispatch", "combine", "PackedTokens", "CudaWorkspace", "MoEBlock", "MoEConfig",
-           "MoEWeights", "make_weights", "capture_forward", "get_extension"]
+           "MoEWeights", "make_weights", "capture_forward", "get_extension", "HostPipeline"]
 _EXPORTS = {
     "dispatch": (".ops", "dispatch"),
     "combine": (".ops", "combine"),
@@ -20,6 +20,7 @@ _EXPORTS = {
     "make_weights": (".layer", "make_weights"),
     "capture_forward": (".graphs", "capture_forward"),
     "get_extension": ("._extension", "get_extension"),
+    "HostPipeline": (".host_pipeline", "HostPipeline"),
 }
 
 

@@ -42,7 +42,7 @@ import ctypes
 import torch
 import torch.distributed as dist
 
-from .layer import MoEConfig
+from .layer import MoEConfig, check_out
 from .workspace import CudaWorkspace, capacity_rows
 from ._extension import get_extension
 
@@ -232,9 +232,11 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         return self._transport[key], self._route[key]
 
     @torch.inference_mode()
-    def forward(self, x, events=None):
+    def forward(self, x, events=None, out=None):
         """`events`, if given, maps stage names ("exchange", "gemm1", "gemm2",
-        "return") to (start, end) CUDA events recorded around those stages."""
+        "return") to (start, end) CUDA events recorded around those stages.
+        `out`, if given, receives the combined rows instead of the workspace's
+        reusable output view."""
         cfg = self.config
 
         def mark(name, which):
@@ -245,6 +247,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             raise ValueError("expected contiguous x[T,hidden]")
         if x.dtype != torch.bfloat16 or x.device != self.gate_up_weight.device:
             raise ValueError("input must be bf16 on the block's device")
+        check_out(out, x)
         ext = self.extension
         transport, (ids32, ids64, weights, logits) = self._state(x)
         tokens = x.shape[0]
@@ -253,7 +256,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             ext.route_out(x, self.router_weight, self.routing_bias, logits, ids32, ids64, weights)
         transport.dispatch(x, ids32, ids64)
         if self.backend == "p2p":
-            return self._forward_p2p(x, transport, weights, mark)
+            return self._forward_p2p(x, transport, weights, mark, out)
         recv_counts = exchange_counts(transport.counts, self.ranks, self.group)
         send_rows, recv_rows = split_sizes(transport.counts, recv_counts, self.ranks)
         self.last_split_sizes = (send_rows, recv_rows)
@@ -282,8 +285,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         exchange_rows(recv[:n_recv], recv_rows, back[:n], send_rows, self.group)
         mark("return", 1)
         if tokens:
-            transport.combine(back[:n], weights)
-        return transport.output
+            return transport.combine(back[:n], weights, out)
+        return transport.output if out is None else out
 
     def _peer_exchange(self, tokens, device):
         cfg = self.config
@@ -309,7 +312,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             self.config.alignment, hidden, grouped_rows, back_rows, self.timeout_ms,
         )
 
-    def _forward_p2p(self, x, transport, weights, mark):
+    def _forward_p2p(self, x, transport, weights, mark, out=None):
         """Steps 3-8 over peer memory: no host synchronisation (graph-capturable)."""
         cfg = self.config
         ext = self.extension
@@ -345,8 +348,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self._p2p(4, None, None)
         mark("return", 1)
         if tokens:
-            transport.combine(ex.back[:n], weights)
-        return transport.output
+            return transport.combine(ex.back[:n], weights, out)
+        return transport.output if out is None else out
 
     def close(self):
         """Release the P2P exchange region (call on every rank, before the process group ends)."""

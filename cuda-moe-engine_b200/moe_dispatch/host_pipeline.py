@@ -1,0 +1,105 @@
+"""Batches held in pinned host memory through a block, copies overlapped with compute.
+
+The reference's block benchmark (block_benchmark.py) times a block on tensors
+already on the GPU; a serving loop around it copies each batch in, runs the
+block and copies the result out, one after the other.  `HostPipeline` keeps
+`slots` device buffers and two copy streams: while batch i computes on the
+caller's stream, batch i+1's host→device copy and batch i-1's device→host copy
+run on the copy engines, so once the pipe is full a step costs
+max(compute, copies) instead of their sum.  Every batch is still copied in and
+out in full; nothing is cached between batches.
+
+Dependencies, per slot s (events on the device, no host synchronisation):
+    load(i)    waits computed[s] of batch i-slots (x[s] free), records loaded[s]
+    compute(i) waits loaded[s] and stored[s] (y[s] free), records computed[s]
+    store(i)   waits computed[s], records stored[s]
+"""
+
+from __future__ import annotations
+
+import torch
+
+
+class HostPipeline:
+    """Run `block(x, out=y)` over pinned host batches of one shape.
+
+    `block` is a `MoEBlock` or an `ExpertParallelMoEBlock` (anything whose
+    forward accepts `out=`).  Host tensors must be pinned, contiguous and of the
+    pipeline's shape and dtype; the caller must not touch them until `run`
+    returns (or, with `synchronize=False`, until the caller's stream has
+    passed the point where `run` returned).
+    """
+
+    def __init__(self, block, tokens, *, hidden=None, dtype=torch.bfloat16, device=None,
+                 slots=2):
+        if slots < 2:
+            raise ValueError("a pipeline needs at least two slots")
+        device = torch.device(device) if device is not None else block.gate_up_weight.device
+        if device.type != "cuda":
+            raise RuntimeError("HostPipeline drives a CUDA block")
+        hidden = hidden or block.config.hidden
+        self.block = block
+        self.shape = (int(tokens), int(hidden))
+        self.dtype = dtype
+        self.device = device
+        self.slots = slots
+        self.x = [torch.empty(self.shape, dtype=dtype, device=device) for _ in range(slots)]
+        self.y = [torch.empty(self.shape, dtype=dtype, device=device) for _ in range(slots)]
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+        self.loaded = [torch.cuda.Event() for _ in range(slots)]
+        self.computed = [torch.cuda.Event() for _ in range(slots)]
+        self.stored = [torch.cuda.Event() for _ in range(slots)]
+
+    def _check(self, tensors, what):
+        for t in tensors:
+            if t.device.type != "cpu" or not t.is_pinned():
+                raise ValueError(f"{what} must be pinned host tensors")
+            if tuple(t.shape) != self.shape or t.dtype != self.dtype or not t.is_contiguous():
+                raise ValueError(f"{what} must be contiguous {self.dtype} tensors of shape "
+                                 f"{self.shape}")
+
+    def bytes_per_batch(self):
+        """(host→device, device→host) bytes copied for one batch."""
+        n = self.shape[0] * self.shape[1] * torch.empty((), dtype=self.dtype).element_size()
+        return n, n
+
+    @torch.inference_mode()
+    def run(self, inputs, outputs, synchronize=True):
+        """outputs[i] = block(inputs[i]) for every i; returns `outputs`."""
+        inputs, outputs = list(inputs), list(outputs)
+        if len(inputs) != len(outputs):
+            raise ValueError("inputs and outputs differ in length")
+        self._check(inputs, "inputs")
+        self._check(outputs, "outputs")
+        compute = torch.cuda.current_stream(self.device)
+        # copies start after whatever the caller queued before this call
+        self.h2d.wait_stream(compute)
+        self.d2h.wait_stream(compute)
+
+        def load(i):
+            s = i % self.slots
+            self.h2d.wait_event(self.computed[s])
+            with torch.cuda.stream(self.h2d):
+                self.x[s].copy_(inputs[i], non_blocking=True)
+            self.loaded[s].record(self.h2d)
+
+        for i in range(min(self.slots - 1, len(inputs))):
+            load(i)
+        for i in range(len(inputs)):
+            s = i % self.slots
+            if i + self.slots - 1 < len(inputs):
+                load(i + self.slots - 1)
+            compute.wait_event(self.loaded[s])
+            compute.wait_event(self.stored[s])
+            self.block(self.x[s], out=self.y[s])
+            self.computed[s].record(compute)
+            self.d2h.wait_event(self.computed[s])
+            with torch.cuda.stream(self.d2h):
+                outputs[i].copy_(self.y[s], non_blocking=True)
+            self.stored[s].record(self.d2h)
+        compute.wait_stream(self.h2d)
+        compute.wait_stream(self.d2h)
+        if synchronize:
+            compute.synchronize()
+        return outputs

@@ -89,6 +89,15 @@ class LayerWorkspace:
     expert_output: torch.Tensor
 
 
+def check_out(out, x):
+    """Reject an explicit output buffer that the combine cannot write as-is."""
+    if out is None:
+        return
+    if (out.shape != x.shape or out.dtype != x.dtype or out.device != x.device
+            or not out.is_contiguous()):
+        raise ValueError("out must be a contiguous tensor with x's shape, dtype and device")
+
+
 class MoEBlock(torch.nn.Module):
     """Inference-only top-k MoE: router, dispatch, two grouped GEMMs with SwiGLU, combine.
 
@@ -206,16 +215,19 @@ class MoEBlock(torch.nn.Module):
         return state.expert_output
 
     @torch.inference_mode()
-    def forward(self, x):
+    def forward(self, x, out=None):
+        """Block output for x[T,hidden].  Without `out` the result is the
+        workspace's reusable output view; with `out` (a contiguous [T,hidden]
+        tensor of x's dtype and device) the combine writes there instead."""
         if x.ndim != 2 or x.shape[1] != self.config.hidden or not x.is_contiguous():
             raise ValueError("expected contiguous x[T,hidden]")
         if x.dtype != self.gate_up_weight.dtype or x.device != self.gate_up_weight.device:
             raise ValueError("input dtype/device must match expert weights")
+        check_out(out, x)
         if x.shape[0] == 0:
-            return torch.empty_like(x)
+            return torch.empty_like(x) if out is None else out
         state = self.workspace(x)
         ids32, ids64, weights = self.route(x)
         state.transport.dispatch(x, ids32, ids64)
         output = self.experts_forward(state)
-        state.transport.combine(output, weights)
-        return state.transport.output
+        return state.transport.combine(output, weights, out)

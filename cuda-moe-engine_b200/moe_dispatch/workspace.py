@@ -89,8 +89,11 @@ class CudaWorkspace:
                 self.vectorized, self.alignment, scratch=self.scratch,
             )
 
-    def combine(self, expert_output, weights):
-        self.extension.combine_out(expert_output, self.inverse, weights, self.output)
+    def combine(self, expert_output, weights, out=None):
+        """Weighted sum of each token's K expert rows into `out` (default: self.output)."""
+        out = self.output if out is None else out
+        self.extension.combine_out(expert_output, self.inverse, weights, out)
+        return out
 
     @property
     def workspace_bytes(self):

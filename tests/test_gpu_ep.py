@@ -92,6 +92,9 @@ def test_single_rank_expert_parallel_block_equals_moeblock(backend, fused_return
         expected = single(x).clone()
         assert torch.equal(ep(x).clone(), expected)
         assert torch.equal(ep(x).clone(), expected)
+        y = torch.full_like(x, float("nan"))
+        assert ep(x, out=y) is y
+        assert torch.equal(y, expected)
         assert ep.extension.device_status() == 0
         ep.close()
     finally:

@@ -101,3 +101,28 @@ def test_block_workload_generators_are_shardable():
     x = block_input(w)
     assert torch.equal(block_input(w, tokens=16, first_token=32), x[32:48])
     assert bias.abs().sum() == 0
+
+
+def test_explicit_output_buffer_is_checked_on_the_host():
+    from moe_dispatch.layer import check_out
+
+    x = torch.zeros(4, 8, dtype=torch.bfloat16)
+    check_out(None, x)
+    check_out(torch.empty_like(x), x)
+    for bad in (torch.empty(5, 8, dtype=torch.bfloat16), torch.empty(4, 8),
+                torch.empty(8, 4, dtype=torch.bfloat16).t()):
+        with pytest.raises(ValueError):
+            check_out(bad, x)
+
+
+def test_host_pipeline_needs_a_cuda_block():
+    from moe_dispatch.host_pipeline import HostPipeline
+
+    class CpuBlock:
+        class config:
+            hidden = 8
+
+    with pytest.raises(RuntimeError):
+        HostPipeline(CpuBlock(), 4, device="cpu")
+    with pytest.raises(ValueError):
+        HostPipeline(CpuBlock(), 4, device="cpu", slots=1)
