@@ -33,6 +33,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 namespace moe {
@@ -802,13 +803,14 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Row-major bf16 matrix [rows, cols], boxes of 128 rows x 64 columns, 128B swizzle.
-bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols) {
+// Row-major bf16 matrix [rows, cols], boxes of box_rows rows x 64 columns, 128B swizzle.
+bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
+                     uint32_t box_rows = kBoxRows) {
     auto encode = tensor_map_encoder();
     if (!encode) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(kBoxRows)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t elem_strides[2] = {1, 1};
     return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                   box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -828,19 +830,53 @@ DeviceInfo& device_info(int device) {
     return infos[device & 63];
 }
 
-// Tile shape selection (MOE_B200_GEMM_TILE=pair|single overrides).  Measured on
-// B200, the 256-row CTA-pair tile wins the plain (down) GEMM once experts hold
-// about 512 rows or more on average (Mixtral 1024 rows/expert: 0.71 vs 0.79 ms;
-// 64 experts x 1536 rows: 0.46 vs 0.52 ms; 256 experts x 1024 rows: 7.13 vs
-// 7.52 ms), because it streams half the weight bytes per output row.  With
-// fewer rows per expert (256 experts x 256 rows: 2.94 vs 2.47 ms) and on the
-// SwiGLU GEMM, whose epilogue halves the tile's output width, the rows it pads
-// above each expert's last multiple of 256 cost more than that saves.
-bool use_pair_tile(int64_t rows, int experts, bool swiglu) {
+enum class Tile { kSingle, kPair };
+
+// Tile shape selection (MOE_B200_GEMM_TILE=single|pair overrides).
+// Measured on B200, the 256-row CTA-pair tile wins the plain (down) GEMM once
+// experts hold about 512 rows or more on average (Mixtral 1024 rows/expert:
+// 0.71 vs 0.79 ms; 64 experts x 1536 rows: 0.46 vs 0.52 ms; 256 experts x
+// 1024 rows: 7.13 vs 7.52 ms), because it streams half the weight bytes per
+// output row.  With fewer rows per expert (256 experts x 256 rows: 2.94 vs
+// 2.47 ms) and on the SwiGLU GEMM, whose epilogue halves the tile's output
+// width, the rows it pads above each expert's last multiple of 256 cost more
+// than that saves.
+Tile pick_tile(int64_t rows, int experts, bool swiglu) {
     const char* env = getenv("MOE_B200_GEMM_TILE");
-    if (env && env[0] == 'p') return true;
-    if (env && env[0] == 's') return false;
-    return !swiglu && rows >= 512 * static_cast<int64_t>(experts);
+    if (env && strcmp(env, "pair") == 0) return Tile::kPair;
+    if (env && strcmp(env, "single") == 0) return Tile::kSingle;
+    return !swiglu && rows >= 512 * static_cast<int64_t>(experts) ? Tile::kPair : Tile::kSingle;
+}
+
+template <typename Kernel>
+cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& resident_clusters,
+                        int sms, int64_t max_tiles, const CUtensorMap& map_a, const CUtensorMap& map_b,
+                        const GemmParams& p, cudaStream_t stream) {
+    cudaLaunchConfig_t config = {};
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeClusterDimension;
+    attribute[0].val.clusterDim.x = 2;
+    attribute[0].val.clusterDim.y = 1;
+    attribute[0].val.clusterDim.z = 1;
+    config.blockDim = dim3(kThreads);
+    config.dynamicSmemBytes = smem_bytes;
+    config.stream = stream;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    if (!configured) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          smem_bytes));
+        configured = true;
+    }
+    if (resident_clusters == 0) {
+        config.gridDim = dim3(sms & ~1);
+        int clusters = 0;
+        MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kernel, &config));
+        resident_clusters = clusters > 0 ? clusters : sms / 2;
+    }
+    const int64_t clusters = max_tiles < resident_clusters ? max_tiles : resident_clusters;
+    config.gridDim = dim3(static_cast<unsigned>(2 * clusters));
+    return cudaLaunchKernelEx(&config, kernel, map_a, map_b, p);
 }
 
 }  // namespace
@@ -877,37 +913,14 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     p.b_rows = static_cast<int>(b_rows);
     p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
 
-    if (use_pair_tile(rows, experts, swiglu)) {
-        auto kernel = swiglu ? grouped_gemm_pair_kernel<true> : grouped_gemm_pair_kernel<false>;
-        cudaLaunchConfig_t config = {};
-        cudaLaunchAttribute attribute[1];
-        attribute[0].id = cudaLaunchAttributeClusterDimension;
-        attribute[0].val.clusterDim.x = 2;
-        attribute[0].val.clusterDim.y = 1;
-        attribute[0].val.clusterDim.z = 1;
-        config.blockDim = dim3(kThreads);
-        config.dynamicSmemBytes = kPairSmemBytes;
-        config.stream = stream;
-        config.attrs = attribute;
-        config.numAttrs = 1;
-        if (!info.pair_configured[swiglu]) {
-            MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              kPairSmemBytes));
-            info.pair_configured[swiglu] = true;
-        }
-        if (info.pair_clusters == 0) {
-            config.gridDim = dim3(info.sms & ~1);
-            int clusters = 0;
-            MOE_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kernel, &config));
-            info.pair_clusters = clusters > 0 ? clusters : info.sms / 2;
-        }
+    const Tile tile = pick_tile(rows, experts, swiglu);
+    if (tile == Tile::kPair) {
         const int64_t max_tiles =
             ((rows + kPairBM - 1) / kPairBM + experts) * static_cast<int64_t>(p.n_tiles);
-        const int64_t clusters = max_tiles < info.pair_clusters ? max_tiles : info.pair_clusters;
-        config.gridDim = dim3(static_cast<unsigned>(2 * clusters));
-        return cudaLaunchKernelEx(&config, kernel, map_a, map_b, p);
+        return launch_pair(swiglu ? grouped_gemm_pair_kernel<true> : grouped_gemm_pair_kernel<false>,
+                           kPairSmemBytes, info.pair_configured[swiglu], info.pair_clusters,
+                           info.sms, max_tiles, map_a, map_b, p, stream);
     }
-
     auto kernel = swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>;
     if (!info.configured[swiglu]) {
         MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));

@@ -25,9 +25,13 @@ pytestmark = [
 SENTINEL = -12345.0
 
 
-@pytest.fixture(autouse=True, params=["single", "pair"])
+TILES = ["single", "pair"]
+
+
+@pytest.fixture(autouse=True, params=TILES)
 def tile(request, monkeypatch):
-    """Run every test with the 128x256 one-CTA tile and the 256x256 CTA-pair tile."""
+    """Run every test with each tile kind: the 128x256 one-CTA tile and the
+    256x256 CTA-pair tile."""
     monkeypatch.setenv("MOE_B200_GEMM_TILE", request.param)
     return request.param
 
@@ -154,3 +158,20 @@ def test_mixtral_shapes_on_column_slices(ext):
                        what="gate/up swiglu")
     hcols = torch.cat([torch.arange(0, 64), torch.arange(hidden - 64, hidden)])
     assert_gemm_close(out[:, hcols], act, down[:, hcols].contiguous(), offsets, what="down")
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+def test_tile_kinds_give_identical_bits(ext, tile, monkeypatch, swiglu):
+    """The launcher picks a tile kind from the problem shape, so every kind
+    must produce the same bits (an expert-parallel rank sees other shapes
+    than one GPU running all experts)."""
+    if tile != "single":
+        pytest.skip("compares all kinds once")
+    a, w, offsets = make_problem([300, 0, 17, 129, 640, 5], 448, 2 * 192, seed=11)
+    results = {}
+    for kind in TILES:
+        monkeypatch.setenv("MOE_B200_GEMM_TILE", kind)
+        results[kind] = run_swiglu(ext, a, w, offsets) if swiglu else run_plain(ext, a, w, offsets)
+    used = int(offsets[-1])
+    for kind in TILES[1:]:
+        assert torch.equal(results[kind][:used], results["single"][:used]), kind
