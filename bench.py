@@ -450,7 +450,10 @@ def run_ours(args, rank, world, local):
     dispatch_ms = statistics.mean(samples["dispatch"])
     combine_ms = statistics.mean(samples["combine"])
     dc_gbs = (dispatch_bytes + combine_bytes) / ((dispatch_ms + combine_ms) / 1e3) / 1e9
-    traffic = profiled_traffic("grouped_gemm_kernel<1>")
+    state = block.workspace(x)
+    tile = block.extension.grouped_gemm_tile(state.transport.packed.shape[0], workload.experts)
+    gemm1_kernel = "grouped_gemm_pair_kernel<1>" if tile == "pair" else "grouped_gemm_kernel<1>"
+    traffic = profiled_traffic(gemm1_kernel)
 
     result = {
         "metric": METRIC,
@@ -480,7 +483,7 @@ def run_ours(args, rank, world, local):
         "dispatch_combine_gbs": round(dc_gbs, 1),
         "dispatch_combine_frac_of_hbm": round(dc_gbs / hbm_peak, 4),
         "roofline": {
-            "kernel": "grouped_gemm_kernel<true> (gate/up + SwiGLU, tcgen05)",
+            "kernel": f"{gemm1_kernel} (gate/up + SwiGLU, tcgen05, {tile} tile)",
             "bound": "tensor",
             "achieved": round(achieved_tflops, 1),
             "peak": tf_peak,

@@ -41,6 +41,7 @@ SIGNATURES = {
     "moe_swiglu": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _I64, _P]),
     "moe_grouped_gemm_swiglu": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "moe_grouped_gemm": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
+    "moe_grouped_gemm_tile": (ctypes.c_int32, [_I64, _I32]),
     "moe_ep_layout": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moe_ep_regroup": (
         ctypes.c_int, [_P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P]
@@ -340,6 +341,10 @@ class Extension:
                    _DTYPE_CODES[source.dtype], target.data_ptr(), counts.data_ptr(),
                    src_start.data_ptr(), dst_start.data_ptr(), offsets.data_ptr(), ranks,
                    experts, source.shape[1], recv_rows, grouped.shape[0], int(bool(grouping)))
+
+    def grouped_gemm_tile(self, rows, experts):
+        """"pair" or "single": the tile the grouped GEMMs pick for this shape."""
+        return "pair" if self.lib.moe_grouped_gemm_tile(int(rows), int(experts)) else "single"
 
     def device_status(self, clear=False):
         """Current device's kernel status word (0 = no bounded wait ran out)."""

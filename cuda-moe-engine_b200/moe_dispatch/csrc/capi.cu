@@ -219,6 +219,10 @@ int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, 
     return grouped_gemm_common(a, weight, offsets, out, rows, n_cols, k_dim, experts, false, stream);
 }
 
+int32_t moe_grouped_gemm_tile(int64_t rows, int32_t experts) {
+    return moe::grouped_gemm_uses_pair(rows, experts) ? 1 : 0;
+}
+
 int moe_ep_layout(const int32_t* counts, int32_t ranks, int32_t experts, int32_t alignment,
                   int32_t* src_start, int32_t* dst_start, int32_t* offsets, void* stream) {
     if (ranks < 1 || experts < 1 || static_cast<int64_t>(ranks) * experts > (1 << 20))

@@ -11,18 +11,22 @@
 // The bf16 rounding of g and u reproduces the reference's materialised bf16
 // projection before its SwiGLU kernel, so fusing does not change results.
 //
-// Structure (one CTA per SM, 192 threads):
+// Structure (one CTA per SM, 320 threads):
 //   warp 0       TMA producer: A tile 128x64 and B tile 256x64 (two 128-row
 //                boxes) per stage, 128-byte swizzle, 4 stages of 48 KiB.
 //   warp 1       TMEM allocator and single-thread MMA issuer:
 //                tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16, fp32
 //                accumulators in TMEM, two 256-column buffers so the epilogue
 //                of one tile overlaps the main loop of the next.
-//   warps 2..5   epilogue: tcgen05.ld 32 lanes x 32 columns, SwiGLU or cast,
-//                masked 16-byte stores (rows past the expert's end are skipped).
-// Tiles are scheduled on the device from `offsets` (no host sync): expert by
-// expert, and inside an expert n-tile by n-tile over its m-tiles, so the CTAs
-// in flight share the expert's A rows and stream each B tile once.
+//   warps 2..9   epilogue, two warps per TMEM lane quarter, each on half of
+//                the tile's columns: tcgen05.ld 32 lanes x 32 columns, SwiGLU
+//                or cast, masked 16-byte stores (rows past the expert's end
+//                are skipped).
+// Tiles are numbered on the device from `offsets` (no host sync): expert by
+// expert, and inside an expert n-tile by n-tile over its m-tiles.  CTAs claim
+// them in that order with an atomic counter as they become free, so the tiles
+// in flight form one compact window: they share the expert's A rows, and each
+// B tile streams from DRAM once.
 //
 // Every mbarrier wait is bounded (globaltimer); when one runs out the kernel
 // records an error in its status word, stops issuing, waits (bounded) for its
@@ -33,6 +37,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -50,18 +55,37 @@ constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kBoxRows = 128;
 constexpr int kBoxBytes = kBoxRows * kBK * 2;
 constexpr int kTmemCols = 2 * kBN;
-constexpr int kThreads = 192;
-constexpr int kEpilogueThreads = 128;
+// Warps 0 and 1 load and issue; warps 2..9 are the epilogue, two per TMEM lane
+// quarter (and so two per SM sub-partition), each taking half of a tile's
+// output columns, so one warp's TMEM loads and SiLU latency hide the other's.
+constexpr int kEpilogueThreads = 256;
+constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kMaxExperts = 1024;
 constexpr uint64_t kWaitLimitNs = 4000000000ull;   // a wait that takes 4 s is an error
 constexpr uint64_t kDrainLimitNs = 200000000ull;   // bounded drain after an error
 
-constexpr int kBarrierBytes = (2 * kStages + 5) * 8;
-constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + (kMaxExperts + 1) * 4;
+constexpr int kTileRing = 4;                      // tiles claimed ahead of the consumers
+constexpr int kBarrierBytes = (2 * kStages + 5 + 2 * kTileRing) * 8;
+constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + kTileRing * 4 +
+                           (kMaxExperts + 1) * 4;
 
 enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1 };
 
 __device__ int32_t g_gemm_status;
+
+// Dynamic tile scheduling.  Each launch owns one slot {claim counter, CTAs
+// finished}: a CTA's producer thread claims the next tile with one atomicAdd,
+// so tiles are handed out in order as SMs become free (no SM idles while
+// another still holds a queue of tiles, and the tiles in flight stay a
+// compact window whose weights and rows are shared in L2).  The last CTA to
+// finish zeroes the slot for its next user.  Eager launches cycle through
+// the first kSchedEagerSlots slots; launches captured into a CUDA graph get
+// the others, so a graph's slot is not handed to eager launches that may run
+// beside it.  Two launches collide only if they run at the same time with
+// hundreds of other launches issued between them.
+constexpr int kSchedEagerSlots = 512;
+constexpr int kSchedCaptureSlots = 512;
+__device__ uint32_t g_tile_sched[kSchedEagerSlots + kSchedCaptureSlots][2];
 
 struct GemmParams {
     const int32_t* offsets;
@@ -73,6 +97,7 @@ struct GemmParams {
     int n_tiles;         // output column tiles
     int b_rows;          // weight rows per expert (2*I for SwiGLU, N otherwise)
     int up_offset;       // row offset of the "up" half inside an expert (SwiGLU)
+    uint32_t* sched;     // this launch's {claim counter, CTAs finished}
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -113,15 +138,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return done != 0;
 }
 
+// The same with cluster-scope acquire: for phases completed by the other CTA
+// of a pair, whose shared-memory writes must be visible after the wait.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
 __device__ __forceinline__ void record_status(int32_t code) { atomicCAS(&g_gemm_status, 0, code); }
 
 // Bounded wait for the phase of `bar` with the given parity.  Returns false
 // when the CTA is aborting (another role gave up) or this wait ran out.
+template <bool kCluster = false>
 __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity,
                                             volatile int* abort_flag, uint64_t limit_ns) {
     const uint64_t start = global_timer();
     for (uint32_t i = 1;; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
         if ((i & 31) == 0) {
             if (*abort_flag) return false;
             if (global_timer() - start > limit_ns) {
@@ -135,7 +175,13 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity,
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t limit_ns) {
-    return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag, limit_ns);
+    return mbar_try_wait(bar, parity) || mbar_wait_slow<false>(bar, parity, abort_flag, limit_ns);
+}
+
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  volatile int* abort_flag, uint64_t limit_ns) {
+    return mbar_try_wait_cluster(bar, parity) ||
+           mbar_wait_slow<true>(bar, parity, abort_flag, limit_ns);
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
@@ -205,6 +251,22 @@ __device__ __forceinline__ float round_bf16(float v) {
     return __bfloat162float(__float2bfloat16_rn(v));
 }
 
+// Next tile of this launch, or -1 once every tile has been claimed.
+__device__ __forceinline__ int claim_tile(uint32_t* sched, int total_tiles) {
+    const uint32_t t = atomicAdd(sched, 1u);
+    return t < static_cast<uint32_t>(total_tiles) ? static_cast<int>(t) : -1;
+}
+
+// Called by one thread per CTA after the CTA's producer stopped claiming:
+// the last CTA of the grid resets the slot.
+__device__ __forceinline__ void finish_schedule(uint32_t* sched) {
+    __threadfence();
+    if (atomicAdd(sched + 1, 1u) == gridDim.x - 1) {
+        atomicExch(sched, 0u);
+        atomicExch(sched + 1, 0u);
+    }
+}
+
 // Tile t -> (expert, m-tile, n-tile).  Tiles are ordered by expert; inside an
 // expert by n-tile, then m-tile.
 __device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int experts, int n_tiles,
@@ -238,9 +300,12 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint64_t* tmem_full = empty + kStages;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* tile_full = drain + 1;
+    uint64_t* tile_empty = tile_full + kTileRing;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_empty + kTileRing);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4);
+    volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
+    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
@@ -276,6 +341,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 mbar_init(&tmem_full[a], 1);
                 mbar_init(&tmem_empty[a], kEpilogueThreads);
             }
+            for (int r = 0; r < kTileRing; ++r) {
+                mbar_init(&tile_full[r], 1);
+                mbar_init(&tile_empty[r], 1 + kEpilogueThreads);  // MMA thread + epilogue
+            }
             mbar_init(drain, 1);
             *abort_flag = 0;
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -299,7 +368,23 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             uint32_t phase = 0;
             uint32_t armed = 0;            // stages armed at least once
             uint32_t last_parity = 0;      // parity of each stage's latest arm
-            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x) {
+            int ring = 0;
+            uint32_t ring_phase = 0;
+            // One claim is kept in reserve, so the atomic's round trip overlaps
+            // the previous tile's loads instead of stalling the pipeline.
+            int next = claim_tile(p.sched, total_tiles);
+            for (;;) {
+                const int t = *abort_flag ? -1 : next;
+                // publish the claim (or the end) to the MMA thread and the epilogue
+                if (!mbar_wait(&tile_empty[ring], ring_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                tile_ring[ring] = t;
+                mbar_arrive(&tile_full[ring]);
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
+                next = claim_tile(p.sched, total_tiles);
                 int e, m, n;
                 decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
                 const int row0 = p.offsets[e] + m * kBM;
@@ -341,9 +426,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             constexpr uint32_t idesc = make_idesc(kBM, kBN);
             int stage = 0;
             uint32_t phase = 0;
-            int local = 0;
+            int ring = 0;
+            uint32_t ring_phase = 0;
             bool issued = false;
-            for (int t = blockIdx.x; t < total_tiles && !*abort_flag; t += gridDim.x, ++local) {
+            for (int local = 0;; ++local) {
+                if (!mbar_wait(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+                const int t = tile_ring[ring];
+                mbar_arrive(&tile_empty[ring]);
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
@@ -383,8 +477,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else {
         // ---------------------------------------------------- epilogue
         const int quarter = warp & 3;  // TMEM lanes this warp may access
-        int local = 0;
-        for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+        const int half = (warp - 2) >> 2;  // which half of the output columns
+        int ring = 0;
+        uint32_t ring_phase = 0;
+        for (int local = 0;; ++local) {
+            if (!mbar_wait(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+            const int t = tile_ring[ring];
+            mbar_arrive(&tile_empty[ring]);
+            if (++ring == kTileRing) {
+                ring = 0;
+                ring_phase ^= 1u;
+            }
+            if (t < 0) break;
             int e, m, n;
             decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
             const int acc = local & 1;
@@ -412,7 +516,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 }
             }
 #pragma unroll 1
-            for (int c = 0; c < kOutTile; c += 32) {
+            for (int c = half * (kOutTile / 2); c < (half + 1) * (kOutTile / 2); c += 32) {
                 uint32_t v[32];
                 uint32_t outw[16];
                 if constexpr (kSwiglu) {
@@ -461,6 +565,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(kTmemCols));
     }
+    if (threadIdx.x == 0) finish_schedule(p.sched);
     if constexpr (kScatter) {
         // the last CTA to finish raises this rank's return flag on every rank
         if (threadIdx.x == 0) {
@@ -495,26 +600,14 @@ constexpr int kPairStages = 6;
 constexpr int kPairTileABytes = kBM * kBK * 2;     // this CTA's 128 rows of A
 constexpr int kPairTileBBytes = kBoxRows * kBK * 2; // this CTA's 128 rows of B
 constexpr int kPairStageBytes = kPairTileABytes + kPairTileBBytes;
-constexpr int kPairBarrierBytes = (2 * kPairStages + 5) * 8;
-constexpr int kPairSmemBytes =
-    1024 + kPairStages * kPairStageBytes + kPairBarrierBytes + 16 + (kMaxExperts + 1) * 4;
+constexpr int kPairBarrierBytes = (2 * kPairStages + 5 + 2 * kTileRing) * 8;
+constexpr int kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + kPairBarrierBytes + 16 +
+                               kTileRing * 4 + (kMaxExperts + 1) * 4;
 constexpr int kPairBM = 2 * kBM;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_id_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t cluster_count_x() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
     return r;
 }
 
@@ -533,6 +626,10 @@ __device__ __forceinline__ void cluster_sync() {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                  : "memory");
+}
+
+__device__ __forceinline__ void st_cluster_s32(uint32_t cluster_addr, int value) {
+    asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(cluster_addr), "r"(value) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
@@ -575,15 +672,16 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     uint64_t* tmem_full = empty + kPairStages;
     uint64_t* tmem_empty = tmem_full + 2;
     uint64_t* drain = tmem_empty + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+    uint64_t* tile_full = drain + 1;
+    uint64_t* tile_empty = tile_full + kTileRing;   // used in the leader only
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tile_empty + kTileRing);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4);
+    volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
+    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
     const bool leader = rank == 0;
-    const int pair = static_cast<int>(cluster_id_x());
-    const int pairs = static_cast<int>(cluster_count_x());
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
     const int k_blocks = (p.k_dim + kBK - 1) / kBK;
 
@@ -617,6 +715,12 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 mbar_init(&tmem_full[a], 1);
                 mbar_init(&tmem_empty[a], 2 * kEpilogueThreads);
             }
+            // tile ring: the leader's producer claims; the leader's MMA thread,
+            // both epilogues and the peer's producer release a slot
+            for (int r = 0; r < kTileRing; ++r) {
+                mbar_init(&tile_full[r], 1);
+                mbar_init(&tile_empty[r], 2 + 2 * kEpilogueThreads);
+            }
             mbar_init(drain, 1);
             *abort_flag = 0;
             asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -639,7 +743,30 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             int stage = 0;
             uint32_t phase = 0;
             uint32_t armed = 0, last_parity = 0;
-            for (int t = pair; t < total_tiles && !*abort_flag; t += pairs) {
+            int ring = 0;
+            uint32_t ring_phase = 0;
+            // the leader keeps one claim in reserve (see the one-CTA kernel)
+            int next = leader ? claim_tile(p.sched, total_tiles) : -1;
+            for (;;) {
+                int t;
+                if (leader) {
+                    t = *abort_flag ? -1 : next;
+                    if (!mbar_wait(&tile_empty[ring], ring_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                    tile_ring[ring] = t;
+                    st_cluster_s32(map_to_cta(smem_u32(const_cast<int*>(&tile_ring[ring])), 1), t);
+                    mbar_arrive(&tile_full[ring]);
+                    mbar_arrive_cluster(map_to_cta(smem_u32(&tile_full[ring]), 1));
+                } else {
+                    if (!mbar_wait_cluster(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+                    t = tile_ring[ring];
+                    mbar_arrive_cluster(map_to_cta(smem_u32(&tile_empty[ring]), 0));
+                }
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
+                if (leader) next = claim_tile(p.sched, total_tiles);
                 int e, m, n;
                 decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
                 const int row0 = p.offsets[e] + m * kPairBM + static_cast<int>(rank) * kBM;
@@ -680,9 +807,18 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             constexpr uint32_t idesc = make_idesc(kPairBM, kBN);
             int stage = 0;
             uint32_t phase = 0;
-            int local = 0;
+            int ring = 0;
+            uint32_t ring_phase = 0;
             bool issued = false;
-            for (int t = pair; t < total_tiles && !*abort_flag; t += pairs, ++local) {
+            for (int local = 0;; ++local) {
+                if (!mbar_wait(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+                const int t = tile_ring[ring];
+                mbar_arrive(&tile_empty[ring]);
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
                 const int acc = local & 1;
                 const uint32_t acc_phase = (local >> 1) & 1;
                 if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
@@ -721,10 +857,20 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else {
         // ---------------------------------------------------- epilogue (both CTAs)
         const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
         const uint32_t leader_empty0 = map_to_cta(smem_u32(&tmem_empty[0]), 0);
         const uint32_t leader_empty1 = map_to_cta(smem_u32(&tmem_empty[1]), 0);
-        int local = 0;
-        for (int t = pair; t < total_tiles; t += pairs, ++local) {
+        int ring = 0;
+        uint32_t ring_phase = 0;
+        for (int local = 0;; ++local) {
+            if (!mbar_wait_cluster(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+            const int t = tile_ring[ring];
+            mbar_arrive_cluster(map_to_cta(smem_u32(&tile_empty[ring]), 0));
+            if (++ring == kTileRing) {
+                ring = 0;
+                ring_phase ^= 1u;
+            }
+            if (t < 0) break;
             int e, m, n;
             decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
             const int acc = local & 1;
@@ -737,7 +883,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
 #pragma unroll 1
-            for (int c = 0; c < kOutTile; c += 32) {
+            for (int c = half * (kOutTile / 2); c < (half + 1) * (kOutTile / 2); c += 32) {
                 uint32_t v[32];
                 uint32_t outw[16];
                 if constexpr (kSwiglu) {
@@ -785,6 +931,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
         asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                      "r"(kTmemCols));
     }
+    if (threadIdx.x == 0) finish_schedule(p.sched);
 }
 
 // ------------------------------------------------------------------ host side
@@ -821,6 +968,7 @@ bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 struct DeviceInfo {
     int sms = 0;
     int pair_clusters = 0;
+    uint32_t* sched = nullptr;  // device address of g_tile_sched
     bool configured[2] = {false, false};
     bool pair_configured[2] = {false, false};
 };
@@ -830,22 +978,40 @@ DeviceInfo& device_info(int device) {
     return infos[device & 63];
 }
 
+// The scheduling slot of the next launch on `stream` (see g_tile_sched).
+cudaError_t schedule_slot(DeviceInfo& info, cudaStream_t stream, uint32_t** slot) {
+    static std::atomic<uint32_t> eager{0}, captured{0};
+    if (!info.sched) {
+        void* base = nullptr;
+        MOE_CUDA_TRY(cudaGetSymbolAddress(&base, g_tile_sched));
+        info.sched = static_cast<uint32_t*>(base);
+    }
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    MOE_CUDA_TRY(cudaStreamIsCapturing(stream, &capture));
+    const uint32_t index = capture == cudaStreamCaptureStatusActive
+                               ? kSchedEagerSlots + captured.fetch_add(1) % kSchedCaptureSlots
+                               : eager.fetch_add(1) % kSchedEagerSlots;
+    *slot = info.sched + 2 * index;
+    return cudaSuccess;
+}
+
 enum class Tile { kSingle, kPair };
 
-// Tile shape selection (MOE_B200_GEMM_TILE=single|pair overrides).
-// Measured on B200, the 256-row CTA-pair tile wins the plain (down) GEMM once
-// experts hold about 512 rows or more on average (Mixtral 1024 rows/expert:
-// 0.71 vs 0.79 ms; 64 experts x 1536 rows: 0.46 vs 0.52 ms; 256 experts x
-// 1024 rows: 7.13 vs 7.52 ms), because it streams half the weight bytes per
-// output row.  With fewer rows per expert (256 experts x 256 rows: 2.94 vs
-// 2.47 ms) and on the SwiGLU GEMM, whose epilogue halves the tile's output
-// width, the rows it pads above each expert's last multiple of 256 cost more
-// than that saves.
-Tile pick_tile(int64_t rows, int experts, bool swiglu) {
+// Tile shape selection (MOE_B200_GEMM_TILE=single|pair overrides).  The
+// 256-row CTA-pair tile streams half the weight bytes per output row, and
+// with claimed tiles and two epilogue warps per lane quarter it keeps the
+// tensor pipe 90-95 % busy.  Measured in SM cycles on B200 (ncu), it wins or
+// ties wherever experts average 512 rows or more (Mixtral gate/up 1.97 M vs
+// 2.08 M, down 0.98 M vs 1.17 M; 64 experts x 1536 rows: 1.34 M vs 1.34 M,
+// 0.69 M vs 0.77 M; 256 experts x 1024 rows: 15.2 M vs 16.2 M, 8.5 M vs
+// 9.4 M).  With 256 rows per expert the rows it pads above each expert's
+// last multiple of 256 make the one-CTA tile as fast or faster (5.12 M vs
+// 4.94 M, 2.89 M vs 2.87 M).
+Tile pick_tile(int64_t rows, int experts) {
     const char* env = getenv("MOE_B200_GEMM_TILE");
     if (env && strcmp(env, "pair") == 0) return Tile::kPair;
     if (env && strcmp(env, "single") == 0) return Tile::kSingle;
-    return !swiglu && rows >= 512 * static_cast<int64_t>(experts) ? Tile::kPair : Tile::kSingle;
+    return rows >= 512 * static_cast<int64_t>(experts) ? Tile::kPair : Tile::kSingle;
 }
 
 template <typename Kernel>
@@ -912,8 +1078,9 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     p.n_tiles = static_cast<int>((n_out + out_tile - 1) / out_tile);
     p.b_rows = static_cast<int>(b_rows);
     p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
+    MOE_CUDA_TRY(schedule_slot(info, stream, &p.sched));
 
-    const Tile tile = pick_tile(rows, experts, swiglu);
+    const Tile tile = pick_tile(rows, experts);
     if (tile == Tile::kPair) {
         const int64_t max_tiles =
             ((rows + kPairBM - 1) / kPairBM + experts) * static_cast<int64_t>(p.n_tiles);
@@ -969,9 +1136,14 @@ cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int3
     p.n_tiles = static_cast<int>((n_out + kBN - 1) / kBN);
     p.b_rows = static_cast<int>(n_out);
     p.up_offset = 0;
+    MOE_CUDA_TRY(schedule_slot(info, stream, &p.sched));
     // every CTA takes part in the completion ticket, so the grid never depends on the rows
     kernel<<<info.sms, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, scatter);
     return cudaGetLastError();
+}
+
+bool grouped_gemm_uses_pair(int64_t rows, int experts) {
+    return pick_tile(rows, experts) == Tile::kPair;
 }
 
 cudaError_t read_gemm_status(int32_t* code, bool clear) {

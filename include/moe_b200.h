@@ -143,6 +143,13 @@ int moe_grouped_gemm_swiglu(const void* packed, const void* gate_up, const int32
 int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, void* out,
                      int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts, void* stream);
 
+/* Which tile the two grouped GEMMs above use for `rows` packed rows over
+ * `experts` experts (no counterpart in the reference): 1 = the 256-row
+ * CTA-pair tile (cta_group::2), 0 = the 128-row one-CTA tile.  Every tile
+ * kind gives the same bits; the choice only changes speed.  The environment
+ * variable MOE_B200_GEMM_TILE=pair|single overrides it. */
+int32_t moe_grouped_gemm_tile(int64_t rows, int32_t experts);
+
 /* ------------------------------------------------------- expert parallel */
 
 /* Receive layout for expert parallelism (no counterpart in the reference,

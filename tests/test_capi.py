@@ -67,3 +67,18 @@ def test_status_word_requires_a_destination():
     lib = load_library()
     assert lib.moe_device_status(None, 0) == 1
     assert ctypes.c_int  # keep ctypes imported for readers of this file
+
+
+def test_tile_choice_follows_rows_per_expert_and_the_override(monkeypatch):
+    lib = load_library()
+    lib.moe_grouped_gemm_tile.restype = ctypes.c_int32
+    lib.moe_grouped_gemm_tile.argtypes = [ctypes.c_int64, ctypes.c_int32]
+    monkeypatch.delenv("MOE_B200_GEMM_TILE", raising=False)
+    assert lib.moe_grouped_gemm_tile(8256, 8) == 1       # Mixtral: ~1032 rows per expert
+    assert lib.moe_grouped_gemm_tile(65536, 256) == 0    # 256 rows per expert
+    assert lib.moe_grouped_gemm_tile(4095, 8) == 0
+    assert lib.moe_grouped_gemm_tile(4096, 8) == 1
+    monkeypatch.setenv("MOE_B200_GEMM_TILE", "single")
+    assert lib.moe_grouped_gemm_tile(8256, 8) == 0
+    monkeypatch.setenv("MOE_B200_GEMM_TILE", "pair")
+    assert lib.moe_grouped_gemm_tile(16, 8) == 1
