@@ -365,11 +365,13 @@ int moe_ep_p2p_down_return(const void* activated, const void* down, void* const*
 
 int moe_device_status(int32_t* code, int32_t clear) {
     if (!code) return fail(MOE_ERR_INVALID, "code must be non-null");
-    int32_t gemm = 0, ep = 0;
+    int32_t gemm = 0, ep = 0, route = 0;
     int status = cuda_status(moe::read_gemm_status(&gemm, clear != 0), "moe_device_status");
     if (status != MOE_OK) return status;
     status = cuda_status(moe::read_ep_status(&ep, clear != 0), "moe_device_status");
-    *code = gemm ? gemm : ep;
+    if (status != MOE_OK) return status;
+    status = cuda_status(moe::read_route_status(&route, clear != 0), "moe_device_status");
+    *code = gemm ? gemm : (ep ? ep : route);
     return status;
 }
 

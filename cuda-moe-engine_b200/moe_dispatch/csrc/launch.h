@@ -41,6 +41,7 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
                                 int64_t rows, int64_t n_out, int64_t k_dim, int experts,
                                 bool swiglu, cudaStream_t stream, const char** error);
 cudaError_t read_gemm_status(int32_t* code, bool clear);
+cudaError_t read_route_status(int32_t* code, bool clear);
 bool grouped_gemm_uses_pair(int64_t rows, int experts);
 
 // Down GEMM whose epilogue returns each result row to its source rank (P2P

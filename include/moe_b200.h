@@ -232,8 +232,10 @@ int moe_ep_p2p_down_return(const void* activated, const void* down, void* const*
 
 /* ------------------------------------------------------------ diagnostics */
 
-/* Reads (and with clear != 0 resets) the current device's status word, which
- * kernels with bounded waits set when a wait runs out.  0 means no error. */
+/* Reads (and with clear != 0 resets) the current device's status words, which
+ * kernels with bounded waits set when a wait runs out.  0 means no error;
+ * 1 a grouped-GEMM pipeline wait, 2 an expert-parallel peer wait, 3 an
+ * expert-parallel capacity overflow, 4 a router copy wait. */
 int moe_device_status(int32_t* code, int32_t clear);
 
 #ifdef __cplusplus
