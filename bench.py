@@ -326,6 +326,10 @@ def run_expert_parallel(args, rank, world, local):
     gemm1_flops = 2.0 * rows * h * 2 * i
     achieved = gemm1_flops / (stage["gemm1"] / 1e3) / 1e12
     crossing = sum(v for r, v in enumerate(send_rows) if r != rank) * h * 2
+    stage_max = {n: max_over_ranks(v, world, device) for n, v in stage.items()}
+    capacity = block.exchange.grouped.shape[0] if block.backend == "p2p" else rows
+    tile = block.extension.grouped_gemm_tile(capacity, workload.experts // world)
+    gemm1_kernel = "grouped_gemm_pair_kernel<1>" if tile == "pair" else "grouped_gemm_kernel<1>"
     ms_per_step = total_ms / args.steps
     if graphed:
         del graph
@@ -356,13 +360,16 @@ def run_expert_parallel(args, rank, world, local):
             "l2": "inputs larger than L2 (expert weights streamed per step)",
         },
         "stage_ms_rank0": {k: round(v, 4) for k, v in stage.items()},
+        "stage_ms_max_over_ranks": {k: round(v, 4) for k, v in stage_max.items()},
         "all_to_all_bytes_out_rank0": crossing,
+        "exchange_gbs_rank0": round(crossing / (stage["exchange"] / 1e3) / 1e9, 1),
         "roofline": {
-            "kernel": "grouped_gemm_kernel<1> (gate/up + SwiGLU, tcgen05), rank 0",
+            "kernel": f"{gemm1_kernel} (gate/up + SwiGLU, tcgen05, {tile} tile), rank 0",
             "bound": "tensor", "achieved": round(achieved, 1), "peak": tf_peak,
             "unit": "TFLOP/s", "frac": round(achieved / tf_peak, 4),
             "peak_kind": f"{peak_kind} burst bf16 (cuBLAS)", "flops_per_launch": gemm1_flops,
             "traffic": None,
+            "traffic_note": "no ncu capture of a multi-rank run (ncu stays on one GPU)",
         },
         "e2e": {
             "value": round(tokens * world / (e2e_ms / 1e3), 1),

@@ -227,8 +227,13 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
     const int64_t rows = dispatch_offsets[experts];
     const int lane = threadIdx.x & 31;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
-    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; r < rows;
-         r += warps) {
+    // Start at the rows for rank me+1 and wrap around: at any moment the ranks
+    // write to different owners (a shifted all-to-all), instead of every rank
+    // writing to owner 0 first.
+    const int64_t rotate = dispatch_offsets[((me + 1) % ranks) * local];
+    for (int64_t v = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; v < rows;
+         v += warps) {
+        const int64_t r = v + rotate < rows ? v + rotate : v + rotate - rows;
         int lo = 0, hi = experts - 1;  // expert of packed row r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -271,8 +276,11 @@ ep_return_rows_kernel(const uint4* __restrict__ results, Regions regions, int32_
     const int64_t rows = st.recv_prefix[segments];
     const int lane = threadIdx.x & 31;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
-    for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; r < rows;
-         r += warps) {
+    // rows are source-major: start at source me+1's rows (shifted all-to-all)
+    const int64_t rotate = st.recv_prefix[((me + 1) % ranks) * local];
+    for (int64_t v = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; v < rows;
+         v += warps) {
+        const int64_t r = v + rotate < rows ? v + rotate : v + rotate - rows;
         int lo = 0, hi = segments - 1;  // last segment starting at or before r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
