@@ -22,7 +22,9 @@ namespace moe {
 namespace {
 
 constexpr int kIndexThreads = 1024;
-constexpr int kScratchHeader = 16;  // int32 words before the chunk table (ticket + pad)
+// int32 words before the chunk table: [0] completion ticket, [1] running count
+// of out-of-range expert ids, [2] that count for the last finished call; pad.
+constexpr int kScratchHeader = 16;
 
 template <int BYTES> struct VecOf;
 template <> struct VecOf<16> { using T = uint4; };
@@ -68,6 +70,8 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
         }
         __syncthreads();
         if (p < n) slots[p] = valid ? base[warp * experts + e] + rank : -1;
+        const unsigned bad = __ballot_sync(0xffffffffu, p < n && !valid);
+        if (bad && lane == 0) atomicAdd(scratch + 1, __popc(bad));
     }
 
     int32_t* ticket = scratch;
@@ -110,7 +114,10 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
             run += running[x];
         }
         if (lane == 31) offsets[experts] = inclusive;
-        if (lane == 0) *ticket = 0;  // ready for the next call
+        if (lane == 0) {
+            scratch[2] = atomicExch(scratch + 1, 0);  // out-of-range ids of this call
+            *ticket = 0;  // ready for the next call
+        }
     }
 }
 

@@ -19,8 +19,9 @@ class PackedTokens:
     workspace: CudaWorkspace
 
 
-def validate_inputs(x, expert_ids, experts):
-    """ops.py:19-39, with the limits lifted to 1..512 experts and top-k 1..32."""
+def validate_inputs(x, expert_ids, experts, check_range=True):
+    """ops.py:19-39, with the limits lifted to 1..512 experts and top-k 1..32.
+    `check_range=False` skips the host-synchronising id range check."""
     if x.ndim != 2 or expert_ids.ndim != 2:
         raise ValueError("expected x[T,H] and expert_ids[T,K]")
     if x.shape[0] != expert_ids.shape[0] or x.shape[1] < 1:
@@ -39,14 +40,26 @@ def validate_inputs(x, expert_ids, experts):
         raise ValueError(f"topk must be 1..{MAX_TOPK}")
     if x.requires_grad:
         raise ValueError("CUDA operators are forward-only; detach inputs or use inference_mode")
-    if expert_ids.numel() and (expert_ids.min().item() < 0 or expert_ids.max().item() >= experts):
+    if check_range and expert_ids.numel() and (
+            expert_ids.min().item() < 0 or expert_ids.max().item() >= experts):
         raise ValueError("expert_ids contains an out-of-range expert")
 
 
 @torch.inference_mode()
-def dispatch(x, expert_ids, experts, *, workspace=None, vectorized=True, alignment=1):
-    """Pack routed tokens by expert. Bounds checks synchronize; validate once for hot loops."""
-    validate_inputs(x, expert_ids, experts)
+def dispatch(x, expert_ids, experts, *, workspace=None, vectorized=True, alignment=1,
+             check_range="host"):
+    """Pack routed tokens by expert.
+
+    check_range="host" (the reference's behaviour, ops.py:38) raises ValueError
+    on an out-of-range id and synchronises.  "device" does not synchronise:
+    such ids are skipped (slot and inverse -1) and counted on the device, in
+    `workspace.invalid_ids_device` (read it with `workspace.invalid_ids()` or
+    `raise_on_invalid_ids`), so the call can be captured in a CUDA graph.
+    "none" skips the count's check entirely (the kernel still skips such ids).
+    """
+    if check_range not in ("host", "device", "none"):
+        raise ValueError("check_range must be host, device or none")
+    validate_inputs(x, expert_ids, experts, check_range=check_range == "host")
     if not x.is_cuda:
         raise RuntimeError("dispatch requires CUDA; the PyTorch reference runs on the CPU")
     expected_shape = (x.shape[0], x.shape[1], experts, expert_ids.shape[1])
@@ -79,3 +92,11 @@ def combine(expert_output, batch, weights):
         raise TypeError("weights must be floating point")
     batch.workspace.combine(expert_output, weights.to(torch.float32))
     return batch.workspace.output
+
+
+def raise_on_invalid_ids(batch):
+    """After dispatch(check_range="device"): raise ValueError if the last
+    dispatch saw out-of-range expert ids (synchronises)."""
+    bad = batch.workspace.invalid_ids()
+    if bad:
+        raise ValueError(f"expert_ids contained {bad} out-of-range expert id(s)")

@@ -89,6 +89,16 @@ class CudaWorkspace:
                 self.vectorized, self.alignment, scratch=self.scratch,
             )
 
+    @property
+    def invalid_ids_device(self):
+        """Device int32 [1]: out-of-range expert ids seen by the last dispatch
+        (written by the index kernel; reading it on the device needs no sync)."""
+        return self.scratch[2:3]
+
+    def invalid_ids(self):
+        """Out-of-range expert ids of the last dispatch (synchronises)."""
+        return int(self.scratch[2].item())
+
     def combine(self, expert_output, weights, out=None):
         """Weighted sum of each token's K expert rows into `out` (default: self.output)."""
         out = self.output if out is None else out

@@ -77,7 +77,9 @@ int64_t moe_dispatch_scratch_bytes(int64_t tokens, int32_t topk, int32_t experts
  * assignment inside its expert), inverse[T*K] (its packed row) and copies
  * each x row to its packed rows; padding rows are zeroed.  The order inside
  * an expert is the stable token-major order of p = t*K + k, deterministic
- * from run to run.  Out-of-range ids get slot and inverse -1.
+ * from run to run.  Out-of-range ids get slot and inverse -1, and int32
+ * word 2 of `scratch` receives how many there were (a device-side range
+ * check: the reference's ops.dispatch checks on the host, ops.py:38).
  * `vectorized` != 0 selects the widest vector copies the row allows.
  * `scratch` must hold moe_dispatch_scratch_bytes() bytes, zeroed once
  * before its first use; the call leaves it ready for the next call. */

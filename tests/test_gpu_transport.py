@@ -127,6 +127,33 @@ def test_out_of_range_ids_are_skipped(ext):
     assert torch.equal(ws.slots.cpu(), slots)
     assert torch.equal(ws.inverse.cpu(), inverse)
     assert int(ws.inverse[0, 1]) == -1 and int(ws.inverse[1, 1]) == -1
+    assert ws.invalid_ids() == 2
+
+
+def test_device_range_check_counts_without_host_sync(ext):
+    """ops.dispatch(check_range="device"): no host check, the index kernel
+    counts out-of-range ids per call (and the count resets between calls)."""
+    from moe_dispatch import ops
+
+    x, ids, _ = transport_case(2500, 128, 16, 4, torch.bfloat16, "uniform", seed=9)
+    bad = ids.clone()
+    bad[7, 1] = 16
+    bad[1000, 0] = -3
+    bad[2499, 3] = 99
+    ws = CudaWorkspace(2500, 128, 16, 4, torch.bfloat16, extension=ext)
+    with pytest.raises(ValueError):
+        ops.dispatch(x.cuda(), bad.cuda(), 16, workspace=ws)
+    batch = ops.dispatch(x.cuda(), bad.cuda(), 16, workspace=ws, check_range="device")
+    assert int(batch.workspace.invalid_ids_device[0]) == 3
+    with pytest.raises(ValueError, match="3 out-of-range"):
+        ops.raise_on_invalid_ids(batch)
+    counts, offsets, slots, inverse = oracle.dispatch_index(bad, 16, 1)
+    assert torch.equal(ws.counts.cpu(), counts) and torch.equal(ws.inverse.cpu(), inverse)
+    batch = ops.dispatch(x.cuda(), ids.cuda(), 16, workspace=ws, check_range="device")
+    assert ws.invalid_ids() == 0
+    ops.raise_on_invalid_ids(batch)
+    with pytest.raises(ValueError):
+        ops.dispatch(x.cuda(), ids.cuda(), 16, workspace=ws, check_range="sometimes")
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32, torch.bfloat16])

@@ -126,3 +126,26 @@ def test_host_pipeline_needs_a_cuda_block():
         HostPipeline(CpuBlock(), 4, device="cpu")
     with pytest.raises(ValueError):
         HostPipeline(CpuBlock(), 4, device="cpu", slots=1)
+
+
+def test_range_check_can_be_left_to_the_device():
+    x = torch.zeros(3, 8)
+    ids = torch.tensor([[0], [5], [1]], dtype=torch.int32)
+    with pytest.raises(ValueError):
+        validate_inputs(x, ids, 4)
+    validate_inputs(x, ids, 4, check_range=False)
+
+
+def test_block_benchmark_cases_and_percentile_follow_the_reference():
+    from moe_dispatch import block_benchmark as bb
+
+    assert len(bb.workload_cases("smoke")) == 2
+    assert len(bb.workload_cases("quick")) == 8
+    assert [t for t, _, _ in bb.workload_cases("model")] == [128, 256]
+    assert bb.percentile([1.0, 2.0, 3.0, 4.0, 5.0], 0.5) == 3.0
+    assert bb.percentile([1.0, 2.0], 0.95) == pytest.approx(1.95)
+    assert bb.percentile([], 0.5) == 0.0
+    hashes = bb.source_hashes()
+    assert "gemm_sm100.cu" in hashes and "layer.py" in hashes and "moe_b200.h" in hashes
+    with pytest.raises(ValueError):
+        bb.workload_cases("everything")
