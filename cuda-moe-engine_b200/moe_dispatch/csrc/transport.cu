@@ -43,6 +43,9 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
     __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // The pack kernel may start now: it reads its token rows, then waits for
+    // this grid (griddepcontrol.wait) before it needs anything computed here.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     for (int i = tid; i < 32 * experts; i += kIndexThreads) hist[i] = 0;
     for (int i = tid; i < experts; i += kIndexThreads) running[i] = 0;
     __syncthreads();
@@ -85,16 +88,42 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
     if (!is_last) return;
     __threadfence();
 
-    for (int x = tid; x < experts; x += kIndexThreads) {
-        int run = 0;
-        for (unsigned c = 0; c < gridDim.x; ++c) {
-            int32_t* cell = chunk_table + static_cast<int64_t>(c) * experts + x;
-            const int v = __ldcg(cell);
-            *cell = run;  // becomes the chunk's base for this expert
-            run += v;
+    // Chunk bases: each warp scans the chunk column of 4 experts at a time,
+    // 32 chunks per step (lane = chunk), all loads of a step issued first.
+    constexpr int kScanExperts = 4;
+    for (int xb = warp * kScanExperts; xb < experts; xb += (kIndexThreads / 32) * kScanExperts) {
+        int carry[kScanExperts] = {};
+        for (unsigned c0 = 0; c0 < gridDim.x; c0 += 32) {
+            const unsigned c = c0 + lane;
+            int v[kScanExperts];
+#pragma unroll
+            for (int j = 0; j < kScanExperts; ++j)
+                v[j] = (c < gridDim.x && xb + j < experts)
+                           ? __ldcg(chunk_table + static_cast<int64_t>(c) * experts + xb + j)
+                           : 0;
+#pragma unroll
+            for (int j = 0; j < kScanExperts; ++j) {
+                int inclusive = v[j];
+#pragma unroll
+                for (int off = 1; off < 32; off <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+                    if (lane >= off) inclusive += y;
+                }
+                if (c < gridDim.x && xb + j < experts)  // becomes the chunk's base for this expert
+                    chunk_table[static_cast<int64_t>(c) * experts + xb + j] = carry[j] + inclusive - v[j];
+                carry[j] += __shfl_sync(0xffffffffu, inclusive, 31);
+            }
         }
-        counts[x] = run;
-        running[x] = alignment > 1 ? (run + alignment - 1) / alignment * alignment : run;
+        if (lane == 0) {
+#pragma unroll
+            for (int j = 0; j < kScanExperts; ++j) {
+                const int x = xb + j;
+                if (x >= experts) break;
+                counts[x] = carry[j];
+                running[x] = alignment > 1 ? (carry[j] + alignment - 1) / alignment * alignment
+                                           : carry[j];
+            }
+        }
     }
     __syncthreads();
     if (warp == 0) {
@@ -130,6 +159,18 @@ pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
             int experts, int64_t row_vecs, int64_t packed_rows) {
     __shared__ int64_t dest[kMaxTopk];
     const int64_t t = blockIdx.x;
+    constexpr int kUnroll = 4;
+    // Launched as a programmatic dependent of the index kernel: the first
+    // slice of this token's row does not depend on it, so load it first.
+    V first[kUnroll];
+    if (t < tokens) {
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int64_t c = threadIdx.x + u * blockDim.x;
+            if (c < row_vecs) first[u] = __ldg(x + t * row_vecs + c);
+        }
+    }
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (t < tokens) {
         if (threadIdx.x < topk) {
             const int64_t p = t * topk + threadIdx.x;
@@ -148,13 +189,13 @@ pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
         }
         __syncthreads();
         const V* src = x + t * row_vecs;
-        constexpr int kUnroll = 4;
         for (int64_t c0 = threadIdx.x; c0 < row_vecs; c0 += kUnroll * blockDim.x) {
             V v[kUnroll];
 #pragma unroll
             for (int u = 0; u < kUnroll; ++u) {
                 const int64_t c = c0 + u * blockDim.x;
-                if (c < row_vecs) v[u] = __ldg(src + c);
+                if (c0 == threadIdx.x) v[u] = first[u];
+                else if (c < row_vecs) v[u] = __ldg(src + c);
             }
             for (int k = 0; k < topk; ++k) {
                 const int64_t d = dest[k];
@@ -203,18 +244,28 @@ combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __re
         ws[threadIdx.x] = weights[p];
     }
     __syncthreads();
+    constexpr int kBatch = 8;  // loads in flight per thread before the adds that use them
     for (int64_t c = threadIdx.x; c < row_vecs; c += blockDim.x) {
         float acc[N];
 #pragma unroll
         for (int i = 0; i < N; ++i) acc[i] = 0.0f;
-        for (int k = 0; k < topk; ++k) {
-            const int64_t r = rows[k];
-            if (r < 0) continue;
-            Pun in;
-            in.v = __ldg(eo + r * row_vecs + c);
-            const float wk = ws[k];
+        for (int k0 = 0; k0 < topk; k0 += kBatch) {
+            Pun in[kBatch];
 #pragma unroll
-            for (int i = 0; i < N; ++i) acc[i] = __fadd_rn(acc[i], __fmul_rn(wk, E::load(in.e[i])));
+            for (int j = 0; j < kBatch; ++j) {
+                const int64_t r = k0 + j < topk ? rows[k0 + j] : -1;
+                if (r >= 0) in[j].v = __ldg(eo + r * row_vecs + c);
+            }
+            // the adds stay in k order, so batching does not change any bit
+#pragma unroll
+            for (int j = 0; j < kBatch; ++j) {
+                if (k0 + j >= topk) break;
+                if (rows[k0 + j] < 0) continue;
+                const float wk = ws[k0 + j];
+#pragma unroll
+                for (int i = 0; i < N; ++i)
+                    acc[i] = __fadd_rn(acc[i], __fmul_rn(wk, E::load(in[j].e[i])));
+            }
         }
         Pun o;
 #pragma unroll
@@ -270,10 +321,19 @@ cudaError_t launch_pack(const void* x, const int32_t* ids, const int32_t* counts
     const int64_t blocks = tokens + (alignment > 1 ? experts : 0);
     if (blocks == 0) return cudaSuccess;
     const int threads = row_vecs >= 256 ? 256 : 128;
-    pack_kernel<V><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(
-        static_cast<const V*>(x), ids, counts, offsets, table, slots, inverse,
-        static_cast<V*>(packed), tokens, topk, experts, row_vecs, packed_rows);
-    return cudaGetLastError();
+    // programmatic dependent launch: may begin before the index kernel ends
+    cudaLaunchConfig_t config = {};
+    cudaLaunchAttribute attribute[1];
+    attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[0].val.programmaticStreamSerializationAllowed = 1;
+    config.gridDim = dim3(static_cast<unsigned>(blocks));
+    config.blockDim = dim3(threads);
+    config.stream = stream;
+    config.attrs = attribute;
+    config.numAttrs = 1;
+    return cudaLaunchKernelEx(&config, pack_kernel<V>, static_cast<const V*>(x), ids, counts,
+                              offsets, table, slots, inverse, static_cast<V*>(packed), tokens,
+                              topk, experts, row_vecs, packed_rows);
 }
 
 template <int DT, int VB>

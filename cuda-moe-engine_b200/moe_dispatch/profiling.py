@@ -3,6 +3,7 @@
     python -m moe_dispatch.profiling --workload mixtral --stage experts --iters 2
     python -m moe_dispatch.profiling --workload small --trace trace.json
     python -m moe_dispatch.profiling --tile-sweep
+    python -m moe_dispatch.profiling --transport
 
 `--stage` runs one stage of the block `--iters` times after one untimed
 forward, so an ncu capture (`-k regex:<kernel> -s 1 -c 1`) sees a warm launch
@@ -186,6 +187,61 @@ def tile_sweep(cases=(("mixtral", 4096), ("fine_grained", 16384), ("expert_paral
 
 
 @torch.inference_mode()
+def transport_sweep(tokens=4096, hidden=4096, experts=64, topk=8, dtype=torch.float16,
+                    repeats=20, stage=None, iters=None):
+    """The transport-only configuration (dispatch + combine, no router or experts):
+    T=4096, H=4096 fp16 rows, E=64, top-8, uniform and Zipf(1.2) expert popularity.
+
+    One JSON line per (popularity, stage) with the median CUDA-event time of
+    `repeats` launches, each after writing a 256 MB buffer so that no input is
+    left in L2, and the achieved algorithmic GB/s: dispatch reads x once and
+    writes n packed rows (+ ids and inverse, n*8 bytes); combine reads the n
+    rows and writes x's shape (+ inverse and weights).  With `stage`
+    ("dispatch" or "combine") it only runs that stage `iters` times (for ncu).
+    """
+    import json
+    import statistics
+
+    from .routing import transport_case
+    from .workspace import CudaWorkspace
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    element = torch.empty((), dtype=dtype).element_size()
+    n = tokens * topk
+    algorithmic = {"dispatch": tokens * hidden * element + n * hidden * element + n * 8,
+                   "combine": n * hidden * element + tokens * hidden * element + n * 8}
+    for popularity in ("uniform", "zipf"):
+        x, ids, weights = transport_case(tokens, hidden, experts, topk, dtype, popularity, seed=0)
+        x, ids32, weights = x.cuda(), ids.to(torch.int32).cuda(), weights.float().cuda()
+        ws = CudaWorkspace(tokens, hidden, experts, topk, dtype)
+        ws.dispatch(x, ids32)
+        expert_output = torch.randn(ws.packed.shape, device="cuda").to(dtype)
+        runs = {"dispatch": lambda: ws.dispatch(x, ids32),
+                "combine": lambda: ws.combine(expert_output, weights)}
+        if stage is not None:
+            for _ in range(iters or 1):
+                runs[stage]()
+            torch.cuda.synchronize()
+            continue
+        for name, fn in runs.items():
+            samples = []
+            for _ in range(repeats):
+                flush.zero_()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record()
+                fn()
+                end.record()
+                torch.cuda.synchronize()
+                samples.append(start.elapsed_time(end))
+            ms = statistics.median(samples)
+            print(json.dumps({"config": "transport", "popularity": popularity, "stage": name,
+                              "us": round(ms * 1e3, 2),
+                              "gbs": round(algorithmic[name] / (ms / 1e3) / 1e9, 1),
+                              "algorithmic_bytes": algorithmic[name]}), flush=True)
+
+
+@torch.inference_mode()
 def export_trace(block, x, destination, repeats=3):
     state = block.workspace(x)
     for _ in range(3):
@@ -221,9 +277,15 @@ def main():
     parser.add_argument("--experts", type=int, default=None)
     parser.add_argument("--trace", default=None)
     parser.add_argument("--tile-sweep", action="store_true")
+    parser.add_argument("--transport", action="store_true",
+                        help="time dispatch and combine at the transport-only configuration")
+    parser.add_argument("--transport-stage", choices=["dispatch", "combine"], default=None)
     args = parser.parse_args()
     if args.tile_sweep:
         tile_sweep()
+        return 0
+    if args.transport or args.transport_stage:
+        transport_sweep(stage=args.transport_stage, iters=args.iters)
         return 0
     block, x = build(args.workload, tokens=args.tokens, experts=args.experts)
     if args.trace:
