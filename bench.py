@@ -20,6 +20,10 @@ dispatch, gate/up GEMM with fused SwiGLU, down GEMM, combine.
              per launch / its mean CUDA-event duration over K eager steps.
   cpu_baseline  the CPU oracle (a C restatement of the reference's path) on a
              bounded token sample of the same workload, rank 0, N=1 only.
+  transport_config  the metric's second half (dispatch+combine HBM GB/s) on its
+             own configuration, transport only: T=4096 H=4096 fp16, E=64, top-8,
+             uniform and Zipf(1.2) popularity, each launch after an L2 flush
+             (N=1 only).
 
 With N > 1 (torchrun, one process per GPU) the block runs expert-parallel:
 the E experts are sharded evenly over the N ranks (rank r owns E/N of them),
@@ -514,7 +518,30 @@ def run_ours(args, rank, world, local):
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(workload, block, x, args.cpu_sample_tokens)
+    if world == 1:
+        result["transport_config"] = transport_config(hbm_peak)
     return result
+
+
+def transport_config(hbm_peak):
+    """The metric's second half on its own configuration (transport only:
+    T=4096, H=4096 fp16, E=64, top-8, uniform and Zipf(1.2) popularity)."""
+    from moe_dispatch.profiling import transport_sweep
+
+    lines = transport_sweep(verbose=False)
+    total = {}
+    for line in lines:
+        entry = total.setdefault(line["popularity"], {"bytes": 0, "us": 0.0})
+        entry["bytes"] += line["algorithmic_bytes"]
+        entry["us"] += line["us"]
+    out = {"workload": "transport only: T=4096 H=4096 fp16, E=64 top-8; each launch after "
+                       "a 256 MB L2 flush, median of 20", "stages": lines}
+    for popularity, entry in total.items():
+        gbs = entry["bytes"] / (entry["us"] / 1e6) / 1e9
+        out[f"dispatch_combine_gbs_{popularity}"] = round(gbs, 1)
+        out[f"frac_of_hbm_{popularity}"] = round(gbs / hbm_peak, 4)
+    out["hbm_peak_gbs"] = hbm_peak
+    return out
 
 
 # --------------------------------------------------------- CPU port (oracle)

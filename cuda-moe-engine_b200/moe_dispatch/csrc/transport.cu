@@ -221,7 +221,7 @@ pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
 
 // combine: out[t] = cast(sum_k (w[t,k] * f32(eo[row_k]))) with every product and
 // partial sum rounded to fp32 (__fmul_rn/__fadd_rn are never contracted to FMA).
-template <int DT, int VB>
+template <int DT, int VB, int KB>
 __global__ void __launch_bounds__(256)
 combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __restrict__ inverse,
                const float* __restrict__ weights, typename VecOf<VB>::T* __restrict__ out,
@@ -244,7 +244,10 @@ combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __re
         ws[threadIdx.x] = weights[p];
     }
     __syncthreads();
-    constexpr int kBatch = 8;  // loads in flight per thread before the adds that use them
+    // KB loads in flight per thread before the adds that use them: 8 for
+    // top-k > 2; 2 for top-k <= 2, where wider batches only cost registers
+    // (and occupancy) without more loads to overlap.
+    constexpr int kBatch = KB;
     for (int64_t c = threadIdx.x; c < row_vecs; c += blockDim.x) {
         float acc[N];
 #pragma unroll
@@ -343,9 +346,14 @@ cudaError_t launch_combine_t(const void* eo, const int32_t* inverse, const float
     using V = typename VecOf<VB>::T;
     const int64_t row_vecs = row_bytes / VB;
     const int threads = row_vecs >= 256 ? 256 : 128;
-    combine_kernel<DT, VB><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
-        static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
-        row_vecs, packed_rows);
+    if (topk <= 2)
+        combine_kernel<DT, VB, 2><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
+            static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
+            row_vecs, packed_rows);
+    else
+        combine_kernel<DT, VB, 8><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
+            static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
+            row_vecs, packed_rows);
     return cudaGetLastError();
 }
 

@@ -188,7 +188,7 @@ def tile_sweep(cases=(("mixtral", 4096), ("fine_grained", 16384), ("expert_paral
 
 @torch.inference_mode()
 def transport_sweep(tokens=4096, hidden=4096, experts=64, topk=8, dtype=torch.float16,
-                    repeats=20, stage=None, iters=None):
+                    repeats=20, stage=None, iters=None, verbose=True):
     """The transport-only configuration (dispatch + combine, no router or experts):
     T=4096, H=4096 fp16 rows, E=64, top-8, uniform and Zipf(1.2) expert popularity.
 
@@ -198,6 +198,7 @@ def transport_sweep(tokens=4096, hidden=4096, experts=64, topk=8, dtype=torch.fl
     writes n packed rows (+ ids and inverse, n*8 bytes); combine reads the n
     rows and writes x's shape (+ inverse and weights).  With `stage`
     ("dispatch" or "combine") it only runs that stage `iters` times (for ncu).
+    Returns the lines as dicts.
     """
     import json
     import statistics
@@ -207,6 +208,7 @@ def transport_sweep(tokens=4096, hidden=4096, experts=64, topk=8, dtype=torch.fl
 
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
     element = torch.empty((), dtype=dtype).element_size()
+    lines = []
     n = tokens * topk
     algorithmic = {"dispatch": tokens * hidden * element + n * hidden * element + n * 8,
                    "combine": n * hidden * element + tokens * hidden * element + n * 8}
@@ -235,10 +237,14 @@ def transport_sweep(tokens=4096, hidden=4096, experts=64, topk=8, dtype=torch.fl
                 torch.cuda.synchronize()
                 samples.append(start.elapsed_time(end))
             ms = statistics.median(samples)
-            print(json.dumps({"config": "transport", "popularity": popularity, "stage": name,
-                              "us": round(ms * 1e3, 2),
-                              "gbs": round(algorithmic[name] / (ms / 1e3) / 1e9, 1),
-                              "algorithmic_bytes": algorithmic[name]}), flush=True)
+            lines.append({"config": "transport", "popularity": popularity, "stage": name,
+                          "us": round(ms * 1e3, 2),
+                          "gbs": round(algorithmic[name] / (ms / 1e3) / 1e9, 1),
+                          "algorithmic_bytes": algorithmic[name]})
+            if verbose:
+                print(json.dumps(lines[-1]), flush=True)
+        del ws, x, ids32, weights, expert_output
+    return lines
 
 
 @torch.inference_mode()
