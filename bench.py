@@ -76,6 +76,8 @@ def parse_args():
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--ep-backend", choices=["p2p", "nccl"], default=None,
                         help="expert-parallel exchange for N > 1 (default p2p up to 8 GPUs)")
+    parser.add_argument("--ep-micro-batches", type=int, default=1,
+                        help="p2p only: token slices pipelined so exchanges overlap the GEMMs")
     return parser.parse_args()
 
 
@@ -216,7 +218,7 @@ def ep_tokens_per_rank(workload, world):
     return workload.tokens, "weak"
 
 
-def build_ep_block(workload, device, rank, world, backend=None):
+def build_ep_block(workload, device, rank, world, backend=None, micro_batches=1):
     """This rank's shard of the workload: all router rows, E/world experts, its tokens."""
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock, expert_range
     from moe_dispatch.layer import MoEConfig
@@ -234,7 +236,10 @@ def build_ep_block(workload, device, rank, world, backend=None):
                       / w.hidden**0.5).to(torch.bfloat16)
         down[e] = (torch.randn(w.hidden, w.intermediate, device=device, generator=ge)
                    / w.intermediate**0.5).to(torch.bfloat16)
-    block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device, backend=backend)
+    if backend == "nccl" or (backend is None and world > 8):
+        micro_batches = 1
+    block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device, backend=backend,
+                                   micro_batches=micro_batches)
     gx = torch.Generator(device=device).manual_seed(3000 + w.seed * 1000 + rank)
     tokens, _ = ep_tokens_per_rank(w, world)
     x = torch.randn(tokens, w.hidden, device=device, generator=gx).to(torch.bfloat16)
@@ -269,7 +274,8 @@ def run_expert_parallel(args, rank, world, local):
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     workload = WORKLOADS[args.workload]
-    block, x = build_ep_block(workload, device, rank, world, args.ep_backend)
+    block, x = build_ep_block(workload, device, rank, world, args.ep_backend,
+                              args.ep_micro_batches)
     tokens, scaling = ep_tokens_per_rank(workload, world)
     stream = torch.cuda.current_stream(device)
     names = ("exchange", "gemm1", "gemm2", "return")
@@ -312,7 +318,8 @@ def run_expert_parallel(args, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
         stage = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in per_step) for n in names}
-        counts = block._transport[(x.shape[0], x.device)].counts.view(world, -1).sum(1).tolist()
+        # stage events cover the first micro-batch: count its rows only
+        counts = block.last_send_counts(lane=0).view(world, -1).sum(1).tolist()
         send_rows = [int(c) for c in counts]
         recv_rows = None
         if block.backend == "nccl":
@@ -323,8 +330,8 @@ def run_expert_parallel(args, rank, world, local):
 
     hbm_peak, tf_peak, _, peak_kind = measured_peaks()
     h, i = workload.hidden, workload.intermediate
-    if recv_rows is None:  # p2p: the grouped span total on this rank
-        rows = int(block.exchange.state[4 + workload.experts + workload.experts // world].item())
+    if recv_rows is None:  # p2p: the first micro-batch's grouped span total on this rank
+        rows = block.last_grouped_rows(lane=0)
     else:
         rows = sum(recv_rows)
     gemm1_flops = 2.0 * rows * h * 2 * i
@@ -358,6 +365,7 @@ def run_expert_parallel(args, rank, world, local):
             "experts": workload.experts, "topk": workload.topk,
             "parallelism": f"ep{world}",
             "exchange": block.backend,
+            "micro_batches": block.micro_batches,
             "timing": ("CUDA graph replay of one expert-parallel step (NVLink peer stores, no "
                        "host sync)" if graphed else
                        "eager steps (one host sync per step for the all-to-all split sizes)"),

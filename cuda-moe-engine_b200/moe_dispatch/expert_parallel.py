@@ -160,6 +160,18 @@ class PeerExchange:
         self.own, self.opened = None, []
 
 
+class _Lane:
+    """One micro-batch's buffers on the P2P path: transport workspace, route
+    outputs, exchange region, GEMM rows and (after the first) its own stream."""
+
+    def __init__(self):
+        self.transport = {}
+        self.route = {}
+        self.exchange = None
+        self.rows = _Buffers()
+        self.stream = None
+
+
 class ExpertParallelMoEBlock(torch.nn.Module):
     """MoE block whose experts are sharded over the ranks of `group`.
 
@@ -172,10 +184,19 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     (moe_ep_p2p_down_return) instead of a separate return copy.  Its stores go
     out one row per lane; at the expert-parallel configuration the separate,
     coalesced copy is faster, so it is off by default.
+
+    micro_batches=m (p2p only) splits the local tokens into m consecutive
+    slices, each with its own exchange region, run on their own streams in a
+    pipeline: slice i sends its rows once slice i-1's rows have arrived (so the
+    copy runs under slice i-1's gate/up GEMM), and starts its GEMMs once slice
+    i-1's down GEMM is done (so slice i-1's results travel back under them).
+    Every rank must use the same m.  GEMM rows are computed independently, so
+    the output bits do not depend on m.
     """
 
     def __init__(self, config, router_weight, gate_up, down, *, group=None, device="cuda",
-                 routing_bias=None, backend=None, timeout_ms=10000, fused_return=False):
+                 routing_bias=None, backend=None, timeout_ms=10000, fused_return=False,
+                 micro_batches=1):
         super().__init__()
         self.config = config if isinstance(config, MoEConfig) else MoEConfig(*config)
         self.group = group
@@ -208,7 +229,37 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self.backend = backend
         self.timeout_ms = int(timeout_ms)
         self.fused_return = bool(fused_return)
-        self.exchange = None
+        self.micro_batches = int(micro_batches)
+        if self.micro_batches < 1 or (self.micro_batches > 1 and backend != "p2p"):
+            raise ValueError("micro_batches must be 1, or >= 1 with the p2p backend")
+        self._lanes = [_Lane() for _ in range(self.micro_batches)]
+        self._outputs = {}
+        self._last_key = None
+        self._last_keys = []
+
+    @property
+    def exchange(self):
+        """The first micro-batch's P2P exchange (None before the first p2p forward)."""
+        return self._lanes[0].exchange if self.backend == "p2p" else None
+
+    def last_send_counts(self, lane=None):
+        """Rows this rank's last forward packed for each global expert (device int32
+        [E]), over all micro-batches or for micro-batch `lane` only."""
+        if self.backend != "p2p":
+            return self._transport[self._last_key].counts
+        picked = range(len(self._last_keys)) if lane is None else [lane]
+        total = None
+        for i in picked:
+            c = self._lanes[i].transport[self._last_keys[i]].counts
+            total = c.clone() if total is None else total + c
+        return total
+
+    def last_grouped_rows(self, lane=None):
+        """Grouped rows this rank's experts received in the last p2p forward, over all
+        micro-batches or for micro-batch `lane` only (synchronises)."""
+        e, e_l = self.config.experts, self.local_experts
+        picked = self._lanes if lane is None else [self._lanes[lane]]
+        return sum(int(ln.exchange.state[4 + e + e_l].item()) for ln in picked)
 
     def _state(self, x):
         key = (x.shape[0], x.device)
@@ -229,7 +280,23 @@ class ExpertParallelMoEBlock(torch.nn.Module):
                 torch.empty(self.ranks, e_l, dtype=torch.int32, device=x.device),
                 torch.empty(e_l + 1, dtype=torch.int32, device=x.device),
             )
+        self._last_key = key
         return self._transport[key], self._route[key]
+
+    def _lane_state(self, lane, x):
+        key = (x.shape[0], x.device)
+        if key not in lane.transport:
+            cfg = self.config
+            lane.transport[key] = CudaWorkspace(x.shape[0], cfg.hidden, cfg.experts, cfg.topk,
+                                                x.dtype, device=x.device, alignment=1)
+            shape = (x.shape[0], cfg.topk)
+            lane.route[key] = (
+                torch.empty(shape, device=x.device, dtype=torch.int32),
+                torch.empty(shape, device=x.device, dtype=torch.int64),
+                torch.empty(shape, device=x.device, dtype=torch.float32),
+                torch.empty((x.shape[0], cfg.experts), device=x.device, dtype=torch.float32),
+            )
+        return key, lane.transport[key], lane.route[key]
 
     @torch.inference_mode()
     def forward(self, x, events=None, out=None):
@@ -248,6 +315,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         if x.dtype != torch.bfloat16 or x.device != self.gate_up_weight.device:
             raise ValueError("input must be bf16 on the block's device")
         check_out(out, x)
+        if self.backend == "p2p":
+            return self._forward_p2p(x, mark, out)
         ext = self.extension
         transport, (ids32, ids64, weights, logits) = self._state(x)
         tokens = x.shape[0]
@@ -255,8 +324,6 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         if tokens:
             ext.route_out(x, self.router_weight, self.routing_bias, logits, ids32, ids64, weights)
         transport.dispatch(x, ids32, ids64)
-        if self.backend == "p2p":
-            return self._forward_p2p(x, transport, weights, mark, out)
         recv_counts = exchange_counts(transport.counts, self.ranks, self.group)
         send_rows, recv_rows = split_sizes(transport.counts, recv_counts, self.ranks)
         self.last_split_sizes = (send_rows, recv_rows)
@@ -288,22 +355,24 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             return transport.combine(back[:n], weights, out)
         return transport.output if out is None else out
 
-    def _peer_exchange(self, tokens, device):
+    def _peer_exchange(self, lane, tokens, device):
+        """The lane's exchange region, (re)created for `tokens` local tokens; a
+        collective over the group (every rank calls it in the same order)."""
         cfg = self.config
         grouped_rows = capacity_rows(self.ranks * tokens * min(cfg.topk, self.local_experts),
                                      self.local_experts, 1, cfg.alignment)
         back_rows = max(tokens * cfg.topk, 1)
-        if self.exchange is not None and self.exchange.shape == (cfg.experts, cfg.hidden,
-                                                                 grouped_rows, back_rows):
-            return self.exchange
-        if self.exchange is not None:
-            self.exchange.close()
-        self.exchange = PeerExchange(self.extension.lib, self.group, self.ranks, self.rank,
+        shape = (cfg.experts, cfg.hidden, grouped_rows, back_rows)
+        if lane.exchange is not None and lane.exchange.shape == shape:
+            return lane.exchange
+        if lane.exchange is not None:
+            lane.exchange.close()
+        lane.exchange = PeerExchange(self.extension.lib, self.group, self.ranks, self.rank,
                                      cfg.experts, cfg.hidden, grouped_rows, back_rows, device)
-        return self.exchange
+        return lane.exchange
 
-    def _p2p(self, op, rows, aux):
-        ex = self.exchange
+    def _p2p(self, op, rows, aux, ex=None):
+        ex = self.exchange if ex is None else ex
         experts, hidden, grouped_rows, back_rows = ex.shape
         self.extension._call(
             ex.state.device, self.extension.lib.moe_ep_p2p, op,
@@ -312,21 +381,75 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             self.config.alignment, hidden, grouped_rows, back_rows, self.timeout_ms,
         )
 
-    def _forward_p2p(self, x, transport, weights, mark, out=None):
-        """Steps 3-8 over peer memory: no host synchronisation (graph-capturable)."""
+    def _forward_p2p(self, x, mark, out=None):
+        """Steps 1-9 over peer memory: no host synchronisation (graph-capturable).
+        With micro_batches > 1 the slices run as the pipeline described in the
+        class docstring; `mark` events cover the first slice only."""
+        tokens = x.shape[0]
+        m = self.micro_batches
+        if m == 1:
+            result, _, _, key = self._lane_forward(self._lanes[0], x, mark, out)
+            self._last_keys = [key]
+            return result
+        if out is None:
+            key = (tokens, x.device)
+            if key not in self._outputs:
+                self._outputs[key] = torch.empty_like(x)
+            out = self._outputs[key]
+        bounds = [tokens * i // m for i in range(m + 1)]
+        main = torch.cuda.current_stream(x.device)
+        start = torch.cuda.Event()
+        start.record(main)
+        received = gemm_done = None
+        finished, keys = [], []
+        for i, lane in enumerate(self._lanes):
+            if i > 0 and lane.stream is None:
+                lane.stream = torch.cuda.Stream(device=x.device)
+            stream = main if i == 0 else lane.stream
+            with torch.cuda.stream(stream):
+                if i > 0:
+                    stream.wait_event(start)
+                _, received, gemm_done, key = self._lane_forward(
+                    lane, x[bounds[i]:bounds[i + 1]], mark if i == 0 else None,
+                    out[bounds[i]:bounds[i + 1]], after_received=received, after_gemm=gemm_done)
+                keys.append(key)
+                if i > 0:
+                    done = torch.cuda.Event()
+                    done.record(stream)
+                    finished.append(done)
+        for done in finished:
+            main.wait_event(done)
+        self._last_keys = keys
+        return out
+
+    def _lane_forward(self, lane, x, mark=None, out=None, after_received=None, after_gemm=None):
+        """One slice on the current stream.  Returns (output, event after its rows
+        arrived, event after its down GEMM, workspace key)."""
         cfg = self.config
         ext = self.extension
+        mark = mark or (lambda name, which: None)
+        stream = torch.cuda.current_stream(x.device)
+        key, transport, (ids32, ids64, weights, logits) = self._lane_state(lane, x)
         tokens = x.shape[0]
         n = tokens * cfg.topk
-        ex = self._peer_exchange(tokens, x.device)
+        if tokens:
+            ext.route_out(x, self.router_weight, self.routing_bias, logits, ids32, ids64, weights)
+        transport.dispatch(x, ids32, ids64)
+        ex = self._peer_exchange(lane, tokens, x.device)
         rows = ex.grouped.shape[0]
-        activated = self._rows.get("activated", rows, cfg.intermediate, x.dtype, x.device)
-        expert_out = self._rows.get("expert_out", rows, cfg.hidden, x.dtype, x.device)
-        self._p2p(0, None, transport.counts)
+        activated = lane.rows.get("activated", rows, cfg.intermediate, x.dtype, x.device)
+        expert_out = lane.rows.get("expert_out", rows, cfg.hidden, x.dtype, x.device)
+        self._p2p(0, None, transport.counts, ex)
+        if after_received is not None:
+            stream.wait_event(after_received)
         mark("exchange", 0)
-        self._p2p(1, transport.packed, transport.offsets)
-        self._p2p(2, None, None)
+        self._p2p(1, transport.packed, transport.offsets, ex)
+        self._p2p(2, None, None, ex)
         mark("exchange", 1)
+        received = torch.cuda.Event()
+        received.record(stream)
+        if after_gemm is not None:
+            stream.wait_event(after_gemm)
         mark("gemm1", 0)
         ext.grouped_gemm_swiglu_out(ex.grouped, self.gate_up_weight, ex.offsets, activated)
         mark("gemm1", 1)
@@ -339,20 +462,27 @@ class ExpertParallelMoEBlock(torch.nn.Module):
                       ex.state.data_ptr(), self.ranks, self.rank, experts, hidden,
                       cfg.intermediate, grouped_rows, back_rows)
             mark("gemm2", 1)
+            gemm_done = torch.cuda.Event()
+            gemm_done.record(stream)
             mark("return", 0)
         else:
             ext.grouped_gemm_out(activated, self.down_weight, ex.offsets, expert_out)
             mark("gemm2", 1)
+            gemm_done = torch.cuda.Event()
+            gemm_done.record(stream)
             mark("return", 0)
-            self._p2p(3, expert_out, None)
-        self._p2p(4, None, None)
+            self._p2p(3, expert_out, None, ex)
+        self._p2p(4, None, None, ex)
         mark("return", 1)
         if tokens:
-            return transport.combine(ex.back[:n], weights, out)
-        return transport.output if out is None else out
+            result = transport.combine(ex.back[:n], weights, out)
+        else:
+            result = transport.output if out is None else out
+        return result, received, gemm_done, key
 
     def close(self):
-        """Release the P2P exchange region (call on every rank, before the process group ends)."""
-        if self.exchange is not None:
-            self.exchange.close()
-            self.exchange = None
+        """Release the P2P exchange regions (call on every rank, before the process group ends)."""
+        for lane in self._lanes:
+            if lane.exchange is not None:
+                lane.exchange.close()
+                lane.exchange = None

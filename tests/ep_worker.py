@@ -30,11 +30,11 @@ def main():
     from moe_dispatch.routing import BlockWorkload, block_input, block_weights
 
     status = 0
-    cases = [(w, b) for w in (BlockWorkload("ep_check", 512, 256, 128, 8, 2, seed=3),
-                              BlockWorkload("ep_check_fine", 768, 128, 64, 64, 6, seed=4,
-                                            router_std=0.02, zipf_bias=1.1))
-             for b in ("p2p", "nccl")]
-    for workload, backend in cases:
+    cases = [(w, b, m) for w in (BlockWorkload("ep_check", 512, 256, 128, 8, 2, seed=3),
+                                 BlockWorkload("ep_check_fine", 768, 128, 64, 64, 6, seed=4,
+                                               router_std=0.02, zipf_bias=1.1))
+             for b, m in (("p2p", 1), ("nccl", 1), ("p2p", 2), ("p2p", 3))]
+    for workload, backend, micro_batches in cases:
         weights, bias = block_weights(workload)
         x = block_input(workload).cuda()
         cfg = MoEConfig(workload.hidden, workload.intermediate, workload.experts, workload.topk)
@@ -45,7 +45,7 @@ def main():
         first, local_experts = expert_range(workload.experts, world, rank)
         ep = ExpertParallelMoEBlock(cfg, weights.router, weights.gate_up[first:first + local_experts],
                                     weights.down[first:first + local_experts], routing_bias=bias,
-                                    backend=backend)
+                                    backend=backend, micro_batches=micro_batches)
         per_rank = workload.tokens // world
         mine = x[rank * per_rank:(rank + 1) * per_rank].contiguous()
         for _ in range(2):  # reuse of the grown buffers
@@ -56,7 +56,8 @@ def main():
         flag = torch.tensor([0 if ok else 1], device="cuda")
         dist.all_reduce(flag)
         if rank == 0:
-            print(f"{workload.name} [{backend}]: world {world}, mismatching ranks "
+            print(f"{workload.name} [{backend}, {micro_batches} micro-batches]: world {world}, "
+                  f"mismatching ranks "
                   f"{int(flag.item())}", flush=True)
         status |= int(flag.item() != 0)
     dist.destroy_process_group()

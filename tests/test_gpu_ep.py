@@ -68,8 +68,10 @@ def _port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("backend,fused_return", [("p2p", True), ("p2p", False), ("nccl", False)])
-def test_single_rank_expert_parallel_block_equals_moeblock(backend, fused_return):
+@pytest.mark.parametrize("backend,fused_return,micro_batches",
+                         [("p2p", True, 1), ("p2p", False, 1), ("nccl", False, 1),
+                          ("p2p", False, 3), ("p2p", True, 2)])
+def test_single_rank_expert_parallel_block_equals_moeblock(backend, fused_return, micro_batches):
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock
     from moe_dispatch.layer import MoEBlock, MoEConfig, MoEWeights
     from moe_dispatch.routing import BlockWorkload, block_input, block_weights
@@ -88,13 +90,23 @@ def test_single_rank_expert_parallel_block_equals_moeblock(backend, fused_return
         single.routing_bias.copy_(bias)
         ep = ExpertParallelMoEBlock(cfg, weights.router, weights.gate_up, weights.down,
                                     routing_bias=bias, backend=backend,
-                                    fused_return=fused_return)
+                                    fused_return=fused_return, micro_batches=micro_batches)
         expected = single(x).clone()
         assert torch.equal(ep(x).clone(), expected)
         assert torch.equal(ep(x).clone(), expected)
         y = torch.full_like(x, float("nan"))
         assert ep(x, out=y) is y
         assert torch.equal(y, expected)
+        counts = torch.bincount(single.route(x)[1].flatten(), minlength=workload.experts)
+        assert torch.equal(ep.last_send_counts().long().cpu(), counts.cpu())
+        if backend == "p2p":
+            from moe_dispatch.graphs import capture_forward
+
+            graph, captured = capture_forward(ep, x)  # every micro-batch stream joins the capture
+            graph.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(captured, expected)
+            del graph
         assert ep.extension.device_status() == 0
         ep.close()
     finally:
