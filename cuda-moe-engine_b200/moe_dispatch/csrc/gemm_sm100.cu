@@ -70,7 +70,7 @@ constexpr uint64_t kDrainLimitNs = 200000000ull;   // bounded drain after an err
 constexpr int kTileRing = 4;                      // tiles claimed ahead of the consumers
 constexpr int kBarrierBytes = (2 * kStages + 5 + 2 * kTileRing) * 8;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + kTileRing * 4 +
-                           (kMaxExperts + 1) * 4;
+                           2 * (kMaxExperts + 1) * 4;
 
 enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1 };
 
@@ -309,6 +309,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
     int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
+    int* offs = mt_prefix + kMaxExperts + 1;  // shared copy of p.offsets: no global load per tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
@@ -321,7 +322,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const int e = e0 + lane;
             int mt = 0;
             if (e < p.experts) {
-                const int rows = p.offsets[e + 1] - p.offsets[e];
+                const int lo = p.offsets[e], hi = p.offsets[e + 1];
+                offs[e] = lo;
+                if (e == p.experts - 1) offs[p.experts] = hi;
+                const int rows = hi - lo;
                 mt = rows > 0 ? (rows + kBM - 1) / kBM : 0;
             }
             int inclusive = mt;
@@ -390,7 +394,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 next = claim_tile(p.sched, total_tiles);
                 int e, m, n;
                 decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
-                const int row0 = p.offsets[e] + m * kBM;
+                const int row0 = offs[e] + m * kBM;
                 const int brow = e * p.b_rows + n * kOutTile;
                 const int brow2 = kSwiglu ? brow + p.up_offset : brow + kBoxRows;
                 bool ok = true;
@@ -498,8 +502,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(p.offsets[e]) + m * kBM + quarter * 32 + lane;
-            bool valid = row < p.offsets[e + 1];
+            const int64_t row = static_cast<int64_t>(offs[e]) + m * kBM + quarter * 32 + lane;
+            bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
             if constexpr (kScatter) {
@@ -606,7 +610,7 @@ constexpr int kPairTileBBytes = kBoxRows * kBK * 2; // this CTA's 128 rows of B
 constexpr int kPairStageBytes = kPairTileABytes + kPairTileBBytes;
 constexpr int kPairBarrierBytes = (2 * kPairStages + 5 + 2 * kTileRing) * 8;
 constexpr int kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + kPairBarrierBytes + 16 +
-                               kTileRing * 4 + (kMaxExperts + 1) * 4;
+                               kTileRing * 4 + 2 * (kMaxExperts + 1) * 4;
 constexpr int kPairBM = 2 * kBM;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -682,6 +686,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
     volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
     int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
+    int* offs = mt_prefix + kMaxExperts + 1;  // shared copy of p.offsets: no global load per tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
@@ -696,7 +701,10 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const int e = e0 + lane;
             int mt = 0;
             if (e < p.experts) {
-                const int rows = p.offsets[e + 1] - p.offsets[e];
+                const int lo = p.offsets[e], hi = p.offsets[e + 1];
+                offs[e] = lo;
+                if (e == p.experts - 1) offs[p.experts] = hi;
+                const int rows = hi - lo;
                 mt = rows > 0 ? (rows + kPairBM - 1) / kPairBM : 0;
             }
             int inclusive = mt;
@@ -773,7 +781,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 if (leader) next = claim_tile(p.sched, total_tiles);
                 int e, m, n;
                 decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
-                const int row0 = p.offsets[e] + m * kPairBM + static_cast<int>(rank) * kBM;
+                const int row0 = offs[e] + m * kPairBM + static_cast<int>(rank) * kBM;
                 const int brow0 = e * p.b_rows + n * kOutTile;
                 const int brow = kSwiglu ? brow0 + (leader ? 0 : p.up_offset)
                                          : brow0 + static_cast<int>(rank) * kBoxRows;
@@ -881,9 +889,9 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(p.offsets[e]) + m * kPairBM +
+            const int64_t row = static_cast<int64_t>(offs[e]) + m * kPairBM +
                                 static_cast<int>(rank) * kBM + quarter * 32 + lane;
-            const bool valid = row < p.offsets[e + 1];
+            const bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
 #pragma unroll 1
