@@ -56,6 +56,18 @@ for _p in (ROOT / "cuda-moe-engine_b200", ROOT):
 import torch  # noqa: E402
 
 METRIC = "MoE-block tokens/s/GPU (H4096 I14336 E8 top2); dispatch+combine HBM GB/s"
+def workload_config(workload, world):
+    """The `config` object both arms print for the single-GPU (or replica) workload."""
+    h, i = workload.hidden, workload.intermediate
+    return {
+        "workload": f"{workload.name}: T={workload.tokens}/GPU H={h} I={i} E={workload.experts} "
+                    f"top{workload.topk}, fp32 router, bf16 experts",
+        "tokens_per_gpu": workload.tokens, "hidden": h, "intermediate": i,
+        "experts": workload.experts, "topk": workload.topk,
+        "parallelism": "replicas" if world > 1 else "single GPU",
+    }
+
+
 def kernels_per_step(experts):
     """Engine kernels per forward: route (1 fused up to 32 experts, else logits + top-k),
     dispatch (index + pack), two grouped GEMMs, combine."""
@@ -488,11 +500,7 @@ def run_ours(args, rank, world, local):
         "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) tokens, N(0,1/fan_in) weights)",
         "config": {
-            "workload": f"{workload.name}: T={tokens}/GPU H={h} I={i} E={workload.experts} "
-                        f"top{workload.topk}, fp32 router, bf16 experts",
-            "tokens_per_gpu": tokens, "hidden": h, "intermediate": i,
-            "experts": workload.experts, "topk": workload.topk,
-            "parallelism": "replicas" if world > 1 else "single GPU",
+            **workload_config(workload, world),
             "timing": "CUDA graph replay of one block forward per step",
             "l2": "inputs larger than L2 (2.8 GB of expert weights streamed per step)",
         },
@@ -595,8 +603,9 @@ def run_reference(args, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(seconds * 1e3, 2), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": f"{workload.name}: H={workload.hidden} I={workload.intermediate} "
-                               f"E={workload.experts} top{workload.topk}",
+        "config": {**workload_config(workload, 1),
+                   "timing": f"CPU: each step runs {sample} of the workload's tokens through the "
+                             "C restatement of the reference's path, all host threads",
                    "sample_tokens_per_step": sample},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": oracle.num_threads(),
                          "kind": "port",
