@@ -345,6 +345,8 @@ cudaError_t launch_combine_t(const void* eo, const int32_t* inverse, const float
                              int64_t packed_rows, cudaStream_t stream) {
     using V = typename VecOf<VB>::T;
     const int64_t row_vecs = row_bytes / VB;
+    // 256-thread CTAs: 512 (one vector per thread) measured slower, 29.7 vs 26.6 us
+    // at top-2 and 62.4 vs 60 us at top-8 for 4096 rows of 8 KB.
     const int threads = row_vecs >= 256 ? 256 : 128;
     if (topk <= 2)
         combine_kernel<DT, VB, 2><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
@@ -412,9 +414,15 @@ cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_
     const int64_t n = tokens * topk;
     const int64_t chunks = n > 0 ? (n + kDispatchChunk - 1) / kDispatchChunk : 1;
     const size_t smem = static_cast<size_t>(65 * experts) * sizeof(int32_t);
-    MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(smem)));
+    static bool configured[64] = {};
+    int device = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&device));
+    if (!configured[device & 63]) {  // once per device, for the largest expert count
+        MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          65 * kMaxDispatchExperts * static_cast<int>(sizeof(int32_t))));
+        configured[device & 63] = true;
+    }
     dispatch_index_kernel<<<static_cast<unsigned>(chunks), kIndexThreads, smem, stream>>>(
         ids, n, experts, alignment, counts, offsets, slots, scratch);
     MOE_CUDA_TRY(cudaGetLastError());
