@@ -55,6 +55,32 @@ def test_abi_version_and_scratch_query():
          "multiples of 8"),
         (lambda lib: lib.moe_grouped_gemm_swiglu(None, None, None, None, 16, 64, 64, 0, None),
          "experts"),
+        (lambda lib: lib.moe_swiglu(None, 5, None, None, 4, 8, None), "dtype"),
+        (lambda lib: lib.moe_swiglu(None, 2, None, None, 4, 8, None), "null"),
+        (lambda lib: lib.moe_dispatch_no_alloc(None, 2, None, None, None, None, None, None,
+                                               1 << 20, 8, 8, 512, 1 << 23, 1, 1, None),
+         "built-in array"),
+        (lambda lib: lib.moe_ep_layout(None, 0, 8, 1, None, None, None, None), "ranks*experts"),
+        (lambda lib: lib.moe_ep_layout(None, 2, 8, 0, None, None, None, None), "alignment"),
+        (lambda lib: lib.moe_ep_layout(None, 2, 8, 8, None, None, None, None), "null"),
+        (lambda lib: lib.moe_ep_regroup(None, 9, None, None, None, None, None, 2, 8, 64, 4, 4, 1,
+                                        None), "dtype"),
+        (lambda lib: lib.moe_ep_regroup(None, 2, None, None, None, None, None, 2, 8, 0, 4, 4, 1,
+                                        None), "regroup shape"),
+        (lambda lib: lib.moe_ep_p2p(0, None, None, None, None, 9, 0, 72, 8, 64, 16, 16, 100,
+                                    None), "ranks"),
+        (lambda lib: lib.moe_ep_p2p(0, None, None, None, None, 2, 2, 8, 8, 64, 16, 16, 100,
+                                    None), "rank out of range"),
+        (lambda lib: lib.moe_ep_p2p(7, None, None, None, None, 2, 0, 8, 8, 64, 16, 16, 100,
+                                    None), "bad op"),
+        (lambda lib: lib.moe_ep_p2p(0, None, None, None, None, 2, 0, 8, 8, 64, 16, 16, 100,
+                                    None), "null"),
+        (lambda lib: lib.moe_ep_p2p_down_return(None, None, None, None, 2, 0, 8, 64, 12, 16, 16,
+                                                None), "down GEMM shape"),
+        (lambda lib: lib.moe_peer_alloc(0, None, None), "peer allocation"),
+        (lambda lib: lib.moe_peer_open(None, None), "null"),
+        (lambda lib: lib.moe_peer_close(None), "null"),
+        (lambda lib: lib.moe_peer_free(None), "null"),
     ],
 )
 def test_invalid_arguments_are_rejected_on_the_host(call, message):
@@ -82,3 +108,17 @@ def test_tile_choice_follows_rows_per_expert_and_the_override(monkeypatch):
     assert lib.moe_grouped_gemm_tile(8256, 8) == 0
     monkeypatch.setenv("MOE_B200_GEMM_TILE", "pair")
     assert lib.moe_grouped_gemm_tile(16, 8) == 1
+
+
+def test_expert_parallel_region_queries_reject_bad_shapes():
+    lib = load_library()
+    assert lib.moe_ep_p2p_region_bytes(9, 72, 64, 16, 16) == -1      # more than 8 ranks
+    assert lib.moe_ep_p2p_region_bytes(3, 8, 64, 16, 16) == -1       # experts not a multiple
+    assert lib.moe_ep_p2p_region_bytes(2, 8, 12, 16, 16) == -1       # hidden not a multiple of 8
+    good = lib.moe_ep_p2p_region_bytes(2, 8, 64, 16, 16)
+    assert good > 0 and good % 1024 == 0
+    grouped = lib.moe_ep_p2p_region_offset(2, 8, 64, 16, 16, 0)
+    back = lib.moe_ep_p2p_region_offset(2, 8, 64, 16, 16, 1)
+    assert 0 < grouped < back < good and grouped % 1024 == 0 and back - grouped >= 16 * 64 * 2
+    assert lib.moe_ep_p2p_region_offset(2, 8, 64, 16, 16, 2) == -1
+    assert lib.moe_ep_p2p_state_words(2, 8) > 0 and lib.moe_ep_p2p_state_words(3, 8) == -1
