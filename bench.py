@@ -30,9 +30,12 @@ the E experts are sharded evenly over the N ranks (rank r owns E/N of them),
 each rank routes its own T tokens (weak scaling), and token rows travel to
 their experts' ranks and back over NVLink peer memory (ExpertParallelMoEBlock,
 backend "p2p": no host sync, so the step is replayed as a CUDA graph;
-`--ep-backend nccl` uses NCCL all-to-all instead, eager, one host sync per step).
+`--ep-backend nccl` uses NCCL all-to-all instead, eager, one host sync per step;
+`--ep-micro-batches m` pipelines m token slices so the exchanges overlap the
+previous slice's GEMMs). `--workload expert_parallel` runs the E=256 block with
+its fixed 32768 tokens per step split over the ranks (strong scaling).
 `--impl reference` times the CPU port of the reference's path instead (rank 0
-only; the other ranks exit without work).
+only; the other ranks exit without work), on the same workload config.
 """
 
 from __future__ import annotations
