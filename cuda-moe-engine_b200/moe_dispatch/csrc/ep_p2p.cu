@@ -29,6 +29,8 @@
 #include "common.cuh"
 #include "launch.h"
 
+#include <cstdlib>
+
 namespace moe {
 namespace {
 
@@ -322,6 +324,17 @@ __global__ void ep_wait_kernel(Regions regions, const int32_t* state_base, int r
     wait_flags(flags, ranks, epoch, limit_ns);
 }
 
+// Grid of the send and return kernels: 4 CTAs per SM of a B200 by default;
+// MOE_B200_EP_COPY_CTAS=n runs them on n CTAs, to leave SMs to a concurrent GEMM.
+unsigned copy_grid() {
+    static const unsigned grid = [] {
+        const char* env = getenv("MOE_B200_EP_COPY_CTAS");
+        const int n = env ? atoi(env) : 0;
+        return static_cast<unsigned>(n > 0 && n <= 148 * 8 ? n : 148 * 4);
+    }();
+    return grid;
+}
+
 Regions to_regions(void* const* regions, int ranks) {
     Regions r = {};
     for (int i = 0; i < ranks; ++i) r.base[i] = static_cast<char*>(regions[i]);
@@ -362,12 +375,12 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
             break;
         }
         case kEpP2pSend:
-            ep_send_rows_kernel<<<148 * 4, kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), aux, r,
+            ep_send_rows_kernel<<<copy_grid(), kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), aux, r,
                                                              state, ranks, me, experts, row_vecs,
                                                              hidden, grouped_rows, back_rows);
             break;
         case kEpP2pReturn:
-            ep_return_rows_kernel<<<148 * 4, kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), r,
+            ep_return_rows_kernel<<<copy_grid(), kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), r,
                                                                state, ranks, me, experts, row_vecs,
                                                                hidden, grouped_rows, back_rows);
             break;
