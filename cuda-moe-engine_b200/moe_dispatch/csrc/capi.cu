@@ -110,11 +110,16 @@ int64_t moe_dispatch_scratch_bytes(int64_t tokens, int32_t topk, int32_t experts
     return moe::dispatch_scratch_bytes(tokens * topk, experts);
 }
 
-int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* counts,
-                 int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse, int64_t tokens,
-                 int64_t hidden, int32_t topk, int32_t experts, int64_t packed_rows,
-                 int32_t alignment, int32_t vectorized, void* scratch, int64_t scratch_bytes,
-                 void* stream) {
+}  // extern "C"
+
+namespace moe {
+
+// Every check moe_dispatch makes on its arguments except the scratch buffer's,
+// so callers that supply the scratch themselves can validate first.
+int check_dispatch_args(const void* x, int32_t dtype, const int32_t* ids, const int32_t* counts,
+                        const int32_t* offsets, const int32_t* slots, const void* packed,
+                        const int32_t* inverse, int64_t tokens, int64_t hidden, int32_t topk,
+                        int32_t experts, int64_t packed_rows, int32_t alignment) {
     if (!valid_dtype(dtype)) return fail(MOE_ERR_INVALID, "only FP32, FP16, and BF16 are supported");
     if (tokens < 0 || hidden < 1) return fail(MOE_ERR_INVALID, "incompatible token dimensions");
     if (topk < 1 || topk > moe::kMaxTopk)
@@ -133,15 +138,34 @@ int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* coun
         return fail(MOE_ERR_INVALID, "incorrect packed workspace: %lld rows, need %s%lld",
                     static_cast<long long>(packed_rows), alignment == 1 ? "" : ">= ",
                     static_cast<long long>(required));
-    if (!counts || !offsets || !scratch || (n > 0 && (!x || !ids || !slots || !packed || !inverse)))
+    if (!counts || !offsets || (n > 0 && (!x || !ids || !slots || !packed || !inverse)))
         return fail(MOE_ERR_INVALID, "null workspace pointer");
+    const int elem = moe::dtype_bytes(dtype);
+    if (!aligned(x, elem) || !aligned(packed, elem))
+        return fail(MOE_ERR_INVALID, "x and packed must be aligned to their element size");
+    return MOE_OK;
+}
+
+}  // namespace moe
+
+extern "C" {
+
+int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* counts,
+                 int32_t* offsets, int32_t* slots, void* packed, int32_t* inverse, int64_t tokens,
+                 int64_t hidden, int32_t topk, int32_t experts, int64_t packed_rows,
+                 int32_t alignment, int32_t vectorized, void* scratch, int64_t scratch_bytes,
+                 void* stream) {
+    const int checked = moe::check_dispatch_args(x, dtype, ids, counts, offsets, slots, packed,
+                                                 inverse, tokens, hidden, topk, experts,
+                                                 packed_rows, alignment);
+    if (checked != MOE_OK) return checked;
+    const int64_t n = tokens * topk;
+    if (!scratch) return fail(MOE_ERR_INVALID, "null workspace pointer");
     if (scratch_bytes < moe::dispatch_scratch_bytes(n, experts) || !aligned(scratch, 16))
         return fail(MOE_ERR_INVALID, "dispatch scratch too small or unaligned (%lld bytes needed)",
                     static_cast<long long>(moe::dispatch_scratch_bytes(n, experts)));
     const int elem = moe::dtype_bytes(dtype);
     const int64_t row_bytes = hidden * elem;
-    if (!aligned(x, elem) || !aligned(packed, elem))
-        return fail(MOE_ERR_INVALID, "x and packed must be aligned to their element size");
     // vectorized: the widest copy the rows allow; otherwise one element per copy
     // (the reference's pack_scalar_kernel, dispatch.cu:36-50).
     const int vb = vectorized ? vector_bytes(row_bytes, elem, {x, packed}) : elem;

@@ -1,14 +1,14 @@
 // moe_dispatch_no_alloc: dispatch for callers that cannot allocate device memory.
 //
 // moe_dispatch needs a few KiB of device scratch (per-chunk expert counts and
-// a completion ticket) that its caller allocates.  Some callers cannot: code
-// running inside a CUDA graph capture, where a new allocation would break the
-// capture; hosts that hand the library a fixed memory budget and forbid any
-// allocation after start-up (real-time or embedded serving loops); and foreign
-// language bindings that see only raw device pointers and have no allocator.
-// This entry point takes the same inputs and outputs as moe_dispatch but keeps
-// its scratch in a fixed array compiled into the library, so it allocates
-// nothing.
+// a completion ticket) that its caller allocates.  Some callers cannot:
+// serving hosts that hand the library a fixed memory budget at start-up and
+// forbid any allocation afterwards (so that memory use is known in advance
+// and no allocation can fail or stall mid-request), and foreign-language
+// bindings that receive only raw device pointers from their host and have no
+// device allocator of their own.  This entry point takes the same inputs and
+// outputs as moe_dispatch but keeps its scratch in a fixed array compiled
+// into the library, so it allocates nothing.
 //
 // The array g_no_alloc_scratch lives in every GPU that loads the library, for
 // as long as the library stays loaded.  Its capacity bounds the problem size:
@@ -19,10 +19,12 @@
 // address up with cudaGetSymbolAddress while that device is current and caches
 // it; make that first call before any stream capture begins.
 //
-// All calls share the one array and it keeps the previous call's contents: the
-// completion ticket is cleared on the stream before every launch.  Calls whose
-// work overlaps on the GPU (different streams, or different threads without
-// ordering) race on the array; serialise them.
+// Arguments are checked before the array is touched, so a rejected call has
+// no effect on the device.  All calls share the one array and it keeps the
+// previous call's contents: the completion ticket is cleared on the stream
+// before every launch.  Calls whose work overlaps on the GPU (different
+// streams, or different threads without ordering) race on the array;
+// serialise them.
 #include "../../../include/moe_b200.h"
 #include "launch.h"
 
@@ -75,9 +77,7 @@ int moe_dispatch_no_alloc(const void* x, int32_t dtype, const int32_t* ids, int3
                           int64_t tokens, int64_t hidden, int32_t topk, int32_t experts,
                           int64_t packed_rows, int32_t alignment, int32_t vectorized,
                           void* stream) {
-    if (tokens < 0 || topk < 1 || experts < 1)
-        return moe_dispatch(x, dtype, ids, counts, offsets, slots, packed, inverse, tokens, hidden,
-                            topk, experts, packed_rows, alignment, vectorized, nullptr, 0, stream);
+    // the size limit first (it needs only the shape), then moe_dispatch's own checks
     const int64_t needed_bytes = moe_dispatch_scratch_bytes(tokens, topk, experts);
     if (needed_bytes > kNoAllocWords * static_cast<int64_t>(sizeof(int32_t))) {
         char message[256];
@@ -89,6 +89,10 @@ int moe_dispatch_no_alloc(const void* x, int32_t dtype, const int32_t* ids, int3
                  static_cast<long long>(kNoAllocWords * sizeof(int32_t)));
         return refuse(MOE_ERR_INVALID, message);
     }
+    const int checked = moe::check_dispatch_args(x, dtype, ids, counts, offsets, slots, packed,
+                                                 inverse, tokens, hidden, topk, experts,
+                                                 packed_rows, alignment);
+    if (checked != MOE_OK) return checked;
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess) return refuse(MOE_ERR_CUDA, "cudaGetDevice failed");
     int32_t* scratch = nullptr;

@@ -72,12 +72,12 @@ constexpr int kBarrierBytes = (2 * kStages + 5 + 2 * kTileRing) * 8;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + kTileRing * 4 +
                            2 * (kMaxExperts + 1) * 4;
 
-enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1 };
+enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusSlotShared = 5 };
 
 __device__ int32_t g_gemm_status;
 
 // Dynamic tile scheduling.  Each launch owns one slot {claim counter, CTAs
-// finished}: a CTA's producer thread claims the next tile with one atomicAdd,
+// finished, CTAs entered}: a CTA's producer thread claims the next tile with one atomicAdd,
 // so tiles are handed out in order as SMs become free (no SM idles while
 // another still holds a queue of tiles, and the tiles in flight stay a
 // compact window whose weights and rows are shared in L2).  The last CTA to
@@ -85,10 +85,14 @@ __device__ int32_t g_gemm_status;
 // the first kSchedEagerSlots slots; launches captured into a CUDA graph get
 // the others, so a graph's slot is not handed to eager launches that may run
 // beside it.  Two launches collide only if they run at the same time with
-// hundreds of other launches issued between them.
+// hundreds of other launches issued between them, or if one captured graph is
+// replayed on two streams at once.  Every CTA counts itself in on entry; a
+// count past the grid size means a second launch is using the slot before the
+// first has released it, and the kernel records status 5 (kStatusSlotShared):
+// the tiles are then split between the two launches and both results are void.
 constexpr int kSchedEagerSlots = 512;
 constexpr int kSchedCaptureSlots = 512;
-__device__ uint32_t g_tile_sched[kSchedEagerSlots + kSchedCaptureSlots][2];
+__device__ uint32_t g_tile_sched[kSchedEagerSlots + kSchedCaptureSlots][4];
 
 struct GemmParams {
     const int32_t* offsets;
@@ -260,12 +264,19 @@ __device__ __forceinline__ int claim_tile(uint32_t* sched, int total_tiles) {
     return t < static_cast<uint32_t>(total_tiles) ? static_cast<int>(t) : -1;
 }
 
+// Called by one thread per CTA on entry: a slot already entered by a whole
+// grid belongs to another launch still in flight.
+__device__ __forceinline__ void enter_schedule(uint32_t* sched) {
+    if (atomicAdd(sched + 2, 1u) >= gridDim.x) record_status(kStatusSlotShared);
+}
+
 // Called by one thread per CTA after the CTA's producer stopped claiming:
 // the last CTA of the grid resets the slot.
 __device__ __forceinline__ void finish_schedule(uint32_t* sched) {
     __threadfence();
     if (atomicAdd(sched + 1, 1u) == gridDim.x - 1) {
         atomicExch(sched, 0u);
+        atomicExch(sched + 2, 0u);
         atomicExch(sched + 1, 0u);
     }
 }
@@ -314,6 +325,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
     const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+    if (threadIdx.x == 32) enter_schedule(p.sched);
 
     // m-tiles per expert -> exclusive prefix (warp 0).
     if (warp == 0) {
@@ -693,6 +705,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const bool leader = rank == 0;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
     const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+    if (threadIdx.x == 32) enter_schedule(p.sched);
 
     // m-tiles (256 rows) per expert -> exclusive prefix (warp 0, both CTAs).
     if (warp == 0) {
@@ -1004,7 +1017,7 @@ cudaError_t schedule_slot(DeviceInfo& info, cudaStream_t stream, uint32_t** slot
     const uint32_t index = capture == cudaStreamCaptureStatusActive
                                ? kSchedEagerSlots + captured.fetch_add(1) % kSchedCaptureSlots
                                : eager.fetch_add(1) % kSchedEagerSlots;
-    *slot = info.sched + 2 * index;
+    *slot = info.sched + 4 * index;
     return cudaSuccess;
 }
 

@@ -97,4 +97,11 @@ cudaError_t launch_ep_p2p_down_return(const void* activated, const void* down, v
 // Sets the calling thread's message returned by moe_last_error().
 void set_last_error(const char* message);
 
+// moe_dispatch's argument checks, except those on the scratch buffer (capi.cu).
+// Returns MOE_OK, or a status with the calling thread's message set.
+int check_dispatch_args(const void* x, int32_t dtype, const int32_t* ids, const int32_t* counts,
+                        const int32_t* offsets, const int32_t* slots, const void* packed,
+                        const int32_t* inverse, int64_t tokens, int64_t hidden, int32_t topk,
+                        int32_t experts, int64_t packed_rows, int32_t alignment);
+
 }  // namespace moe

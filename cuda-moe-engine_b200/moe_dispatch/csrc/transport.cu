@@ -5,7 +5,7 @@
 // assigns slots with atomicAdd, so its order inside an expert changes from run
 // to run; here the order is the stable token-major order of p = t*K + k:
 //
-//   dispatch_index_kernel  one CTA per 4096 assignments.  match_any groups a
+//   dispatch_index_kernel  one CTA per kDispatchChunk (1024) assignments.  match_any groups a
 //                          warp's assignments by expert, per-warp histograms
 //                          are scanned in warp order, so each assignment gets
 //                          its rank inside the chunk without atomics.  The last

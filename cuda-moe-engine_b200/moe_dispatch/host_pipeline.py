@@ -9,6 +9,12 @@ run on the copy engines, so once the pipe is full a step costs
 max(compute, copies) instead of their sum.  Every batch is still copied in and
 out in full; nothing is cached between batches.
 
+With ``graphs=True`` each slot's forward is captured once as a CUDA graph
+(after a warm-up on that slot's buffers) and replayed, so a step costs one
+graph launch on the host instead of the block's per-kernel launches; the
+block must be capturable (MoEBlock, or ExpertParallelMoEBlock on the p2p
+backend).  The bits are those of the eager forward.
+
 Dependencies, per slot s (events on the device, no host synchronisation):
     load(i)    waits computed[s] of batch i-slots (x[s] free), records loaded[s]
     compute(i) waits loaded[s] and stored[s] (y[s] free), records computed[s]
@@ -31,7 +37,7 @@ class HostPipeline:
     """
 
     def __init__(self, block, tokens, *, hidden=None, dtype=torch.bfloat16, device=None,
-                 slots=2):
+                 slots=2, graphs=False):
         if slots < 2:
             raise ValueError("a pipeline needs at least two slots")
         device = torch.device(device) if device is not None else block.gate_up_weight.device
@@ -43,13 +49,41 @@ class HostPipeline:
         self.dtype = dtype
         self.device = device
         self.slots = slots
-        self.x = [torch.empty(self.shape, dtype=dtype, device=device) for _ in range(slots)]
+        self.x = [torch.zeros(self.shape, dtype=dtype, device=device) for _ in range(slots)]
         self.y = [torch.empty(self.shape, dtype=dtype, device=device) for _ in range(slots)]
         self.h2d = torch.cuda.Stream(device)
         self.d2h = torch.cuda.Stream(device)
         self.loaded = [torch.cuda.Event() for _ in range(slots)]
         self.computed = [torch.cuda.Event() for _ in range(slots)]
         self.stored = [torch.cuda.Event() for _ in range(slots)]
+        self.graphs = self._capture() if graphs else None
+
+    @torch.inference_mode()
+    def _capture(self):
+        """One CUDA graph per slot of block(x[s], out=y[s]), captured on a side
+        stream after a warm-up forward on the same buffers."""
+        compute = torch.cuda.current_stream(self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(compute)
+        with torch.cuda.stream(side):
+            for s in range(self.slots):
+                self.block(self.x[s], out=self.y[s])
+        compute.wait_stream(side)
+        graphs = []
+        for s in range(self.slots):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                self.block(self.x[s], out=self.y[s])
+            graphs.append(graph)
+        compute.wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        return graphs
+
+    def close(self):
+        """Release the captured graphs (before the block's resources go)."""
+        if self.graphs is not None:
+            torch.cuda.synchronize(self.device)
+            self.graphs = None
 
     def _check(self, tensors, what):
         for t in tensors:
@@ -92,7 +126,10 @@ class HostPipeline:
                 load(i + self.slots - 1)
             compute.wait_event(self.loaded[s])
             compute.wait_event(self.stored[s])
-            self.block(self.x[s], out=self.y[s])
+            if self.graphs is not None:
+                self.graphs[s].replay()
+            else:
+                self.block(self.x[s], out=self.y[s])
             self.computed[s].record(compute)
             self.d2h.wait_event(self.computed[s])
             with torch.cuda.stream(self.d2h):

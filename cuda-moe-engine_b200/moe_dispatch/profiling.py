@@ -2,7 +2,6 @@
 
     python -m moe_dispatch.profiling --workload mixtral --stage experts --iters 2
     python -m moe_dispatch.profiling --workload small --trace trace.json
-    python -m moe_dispatch.profiling --tile-sweep
     python -m moe_dispatch.profiling --transport
 
 `--stage` runs one stage of the block `--iters` times after one untimed
@@ -68,122 +67,6 @@ def run_stage(block, x, stage, iters):
         actions[stage]()
     torch.cuda.synchronize()
     return ext.device_status()
-
-
-class ClockProbe:
-    """Median SM clock (MHz) and board power (W) over a code region, read
-    through NVML every 5 ms by a background thread (read-only queries)."""
-
-    def __init__(self, device_index):
-        self.index = device_index
-        self.samples = []
-
-    def __enter__(self):
-        import threading
-
-        import pynvml
-
-        pynvml.nvmlInit()
-        uuid = str(torch.cuda.get_device_properties(self.index).uuid)
-        handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
-        self._stop = threading.Event()
-
-        def sample():
-            while not self._stop.is_set():
-                self.samples.append((pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM),
-                                     pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0))
-                self._stop.wait(0.005)
-
-        self._thread = threading.Thread(target=sample, daemon=True)
-        self._thread.start()
-        return self
-
-    def __exit__(self, *exc):
-        self._stop.set()
-        self._thread.join()
-
-    def summary(self):
-        import statistics
-
-        if not self.samples:
-            return None, None
-        return (statistics.median(c for c, _ in self.samples),
-                round(statistics.median(w for _, w in self.samples), 1))
-
-
-@torch.inference_mode()
-def tile_sweep(cases=(("mixtral", 4096), ("fine_grained", 16384), ("expert_parallel", 8192),
-                      ("expert_parallel", 32768)), warmup=3, iters=10, sustain_s=0.4):
-    """Time both grouped GEMMs with each tile kind (JSON lines).
-
-    Besides the event time of `iters` back-to-back launches, each line carries
-    the median SM clock and board power over a `sustain_s` loop of the same
-    launches, and kcycles = ms x MHz, the clock-independent cost: at this
-    board's power cap a kernel that keeps the tensor pipe busier draws more
-    power and runs at a lower clock.
-    """
-    import json
-    import os
-    import time
-
-    previous = os.environ.get("MOE_B200_GEMM_TILE")
-    try:
-        for name, tokens in cases:
-            block, x = build(name, tokens=tokens)
-            block(x)
-            state = block.workspace(x)
-            t = state.transport
-            ext = block.extension
-            ids32, ids64, _ = block.route(x)
-            t.dispatch(x, ids32, ids64)
-            counts = t.counts.float().cpu()
-            cfg = block.config
-            n = tokens * cfg.topk
-            stages = {
-                "gate_up_swiglu": (lambda: ext.grouped_gemm_swiglu_out(
-                    t.packed, block.gate_up_weight, t.offsets, state.activated),
-                    2 * n * cfg.hidden * 2 * cfg.intermediate),
-                "down": (lambda: ext.grouped_gemm_out(
-                    state.activated, block.down_weight, t.offsets, state.expert_output),
-                    2 * n * cfg.intermediate * cfg.hidden),
-            }
-            for tile in ("single", "pair"):
-                os.environ["MOE_B200_GEMM_TILE"] = tile
-                for stage, (fn, flops) in stages.items():
-                    for _ in range(warmup):
-                        fn()
-                    torch.cuda.synchronize()
-                    start = torch.cuda.Event(enable_timing=True)
-                    end = torch.cuda.Event(enable_timing=True)
-                    start.record()
-                    for _ in range(iters):
-                        fn()
-                    end.record()
-                    torch.cuda.synchronize()
-                    ms = start.elapsed_time(end) / iters
-                    repeats = max(1, int(sustain_s * 1e3 / ms))
-                    with ClockProbe(torch.cuda.current_device()) as probe:
-                        t0 = time.perf_counter()
-                        for _ in range(repeats):
-                            fn()
-                        torch.cuda.synchronize()
-                        sustained_ms = (time.perf_counter() - t0) * 1e3 / repeats
-                    mhz, watts = probe.summary()
-                    print(json.dumps({"workload": name, "tokens": tokens, "tile": tile,
-                                      "gemm": stage, "ms": round(ms, 4),
-                                      "tflops": round(flops / ms / 1e9, 1),
-                                      "sustained_ms": round(sustained_ms, 4),
-                                      "sm_mhz": mhz, "watts": watts,
-                                      "kcycles": round(sustained_ms * mhz, 1) if mhz else None,
-                                      "rows_per_expert_mean": float(counts.mean()),
-                                      "rows_per_expert_max": float(counts.max())}), flush=True)
-            del block, x, state, t
-            torch.cuda.empty_cache()
-    finally:
-        if previous is None:
-            os.environ.pop("MOE_B200_GEMM_TILE", None)
-        else:
-            os.environ["MOE_B200_GEMM_TILE"] = previous
 
 
 @torch.inference_mode()
@@ -282,14 +165,10 @@ def main():
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--experts", type=int, default=None)
     parser.add_argument("--trace", default=None)
-    parser.add_argument("--tile-sweep", action="store_true")
     parser.add_argument("--transport", action="store_true",
                         help="time dispatch and combine at the transport-only configuration")
     parser.add_argument("--transport-stage", choices=["dispatch", "combine"], default=None)
     args = parser.parse_args()
-    if args.tile_sweep:
-        tile_sweep()
-        return 0
     if args.transport or args.transport_stage:
         transport_sweep(stage=args.transport_stage, iters=args.iters)
         return 0

@@ -7,6 +7,8 @@ block inputs and weights for the named block shapes.
 """
 
 import math
+import os
+from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass
 
 import torch
@@ -70,6 +72,22 @@ WORKLOADS = {
 }
 
 
+def block_router(workload):
+    """Router [E,H] fp32 and routing bias [E] of `workload` (the first draws of
+    block_weights, from their own generator)."""
+    w = workload
+    g = torch.Generator().manual_seed(w.seed * 1_000_003 + 17)
+    if w.router_std > 0:
+        router = torch.randn(w.experts, w.hidden, generator=g) * w.router_std
+    else:
+        router = torch.randn(w.experts, w.hidden, generator=g) / math.sqrt(w.hidden)
+    bias = torch.zeros(w.experts)
+    if w.zipf_bias > 0:
+        rank = torch.randperm(w.experts, generator=g).float() + 1.0
+        bias = -w.zipf_bias * torch.log(rank)
+    return router, bias
+
+
 def block_weights(workload, experts=None, first_expert=0):
     """Weights of `workload` on the CPU (bf16 experts, fp32 router).
 
@@ -81,23 +99,23 @@ def block_weights(workload, experts=None, first_expert=0):
 
     w = workload
     experts = w.experts if experts is None else experts
-    g = torch.Generator().manual_seed(w.seed * 1_000_003 + 17)
-    if w.router_std > 0:
-        router = torch.randn(w.experts, w.hidden, generator=g) * w.router_std
-    else:
-        router = torch.randn(w.experts, w.hidden, generator=g) / math.sqrt(w.hidden)
-    bias = torch.zeros(w.experts)
-    if w.zipf_bias > 0:
-        rank = torch.randperm(w.experts, generator=g).float() + 1.0
-        bias = -w.zipf_bias * torch.log(rank)
+    router, bias = block_router(w)
     gate_up = torch.empty(experts, 2 * w.intermediate, w.hidden, dtype=torch.bfloat16)
     down = torch.empty(experts, w.hidden, w.intermediate, dtype=torch.bfloat16)
-    for local in range(experts):
+
+    def draw(local):
         ge = torch.Generator().manual_seed(w.seed * 1_000_003 + 1000 + first_expert + local)
         gate_up[local] = (torch.randn(2 * w.intermediate, w.hidden, generator=ge)
                           / math.sqrt(w.hidden)).to(torch.bfloat16)
         down[local] = (torch.randn(w.hidden, w.intermediate, generator=ge)
                        / math.sqrt(w.intermediate)).to(torch.bfloat16)
+
+    # every expert has its own generator, so drawing them on several threads
+    # gives the same bytes as drawing them in order
+    workers = max(1, min(experts, len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity")
+                         else (os.cpu_count() or 1)))
+    with ThreadPoolExecutor(max_workers=workers) as pool:
+        list(pool.map(draw, range(experts)))
     return MoEWeights(router, gate_up, down), bias
 
 

@@ -89,16 +89,17 @@ int moe_dispatch(const void* x, int32_t dtype, const int32_t* ids, int32_t* coun
                  int32_t alignment, int32_t vectorized, void* scratch, int64_t scratch_bytes,
                  void* stream);
 
-/* moe_dispatch for callers that cannot allocate device memory -- code inside a
- * CUDA graph capture, hosts that forbid allocation after start-up, bindings
- * that hold only raw device pointers.  No counterpart in the reference: its
+/* moe_dispatch for callers that cannot allocate device memory -- serving hosts
+ * that fix their device memory at start-up and forbid allocation afterwards,
+ * bindings that hold only raw device pointers.  No counterpart in the reference: its
  * dispatch needs no scratch because its order is whatever atomics give.
  * Same arguments and results as moe_dispatch, minus the scratch: that lives in
  * a fixed array compiled into the library (256 KiB + 64 B on every GPU that
  * loads it, until exit), which limits the size to
  *   ceil(tokens * topk / 1024) * experts <= 65536
  * (e.g. 262144 assignments over 256 experts); larger requests fail with
- * MOE_ERR_INVALID.  Allocates nothing (no cudaMalloc/cudaFree).  The first
+ * MOE_ERR_INVALID.  Arguments are checked before the array is touched, so a
+ * rejected call has no device effect.  Allocates nothing (no cudaMalloc/cudaFree).  The first
  * call on a device looks up the array's device address; make it before any
  * stream capture.  All calls share the array: calls that overlap on the GPU
  * race and must be serialised by the caller. */
@@ -237,7 +238,10 @@ int moe_ep_p2p_down_return(const void* activated, const void* down, void* const*
 /* Reads (and with clear != 0 resets) the current device's status words, which
  * kernels with bounded waits set when a wait runs out.  0 means no error;
  * 1 a grouped-GEMM pipeline wait, 2 an expert-parallel peer wait, 3 an
- * expert-parallel capacity overflow, 4 a router copy wait. */
+ * expert-parallel capacity overflow, 4 a router copy wait, 5 two grouped-GEMM
+ * launches that shared one tile-claim slot at the same time (one captured
+ * graph replayed on two streams at once, or more than 512 captured GEMM
+ * launches in flight together); their results are void. */
 int moe_device_status(int32_t* code, int32_t clear);
 
 #ifdef __cplusplus

@@ -26,8 +26,12 @@ def test_reference_arm_prints_one_contract_line():
     assert d["impl"] == "reference" and d["metric"] == bench.METRIC
     assert d["unit"] == "tokens/s" and d["higher_is_better"] is True and d["value"] > 0
     assert d["steps"] == 1 and d["warmup"] == 0 and d["n_gpus"] == 1
-    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
+    installed = (ROOT / "baseline" / "_ref" / "moe_dispatch").exists()
+    assert d["cpu_baseline"]["kind"] == ("reference_torch" if installed else "port")
+    assert d["cpu_baseline"]["cores"] == bench.host_threads()
     assert d["cpu_baseline"]["value"] == d["value"]
+    assert d["cpu_baseline"]["port"]["value"] > 0
+    assert "unavailable" in d["reference_gpu"]  # no GPU here
     assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
     from moe_dispatch.routing import WORKLOADS
@@ -59,3 +63,16 @@ def test_expert_parallel_token_split():
 
     assert bench.ep_tokens_per_rank(WORKLOADS["mixtral"], 4) == (4096, "weak")
     assert bench.ep_tokens_per_rank(WORKLOADS["expert_parallel"], 8) == (4096, "strong")
+
+
+def test_reference_package_is_imported_beside_ours():
+    """The reference's package loads under its own name and leaves this
+    engine's moe_dispatch in place."""
+    if not (ROOT / "baseline" / "_ref" / "moe_dispatch").exists():
+        pytest.skip("baseline/_ref not installed")
+    import moe_dispatch
+
+    ref = bench.reference_package()
+    assert ref.__name__ == bench.REFERENCE_ALIAS
+    assert Path(ref.__file__).resolve().is_relative_to(ROOT / "baseline" / "_ref")
+    assert Path(moe_dispatch.__file__).resolve().is_relative_to(ROOT / "cuda-moe-engine_b200")

@@ -60,6 +60,9 @@ def test_abi_version_and_scratch_query():
         (lambda lib: lib.moe_dispatch_no_alloc(None, 2, None, None, None, None, None, None,
                                                1 << 20, 8, 8, 512, 1 << 23, 1, 1, None),
          "built-in array"),
+        # arguments are checked before the built-in array is looked up or cleared
+        (lambda lib: lib.moe_dispatch_no_alloc(None, 5, None, None, None, None, None, None,
+                                               16, 8, 2, 8, 32, 1, 1, None), "FP32"),
         (lambda lib: lib.moe_ep_layout(None, 0, 8, 1, None, None, None, None), "ranks*experts"),
         (lambda lib: lib.moe_ep_layout(None, 2, 8, 0, None, None, None, None), "alignment"),
         (lambda lib: lib.moe_ep_layout(None, 2, 8, 8, None, None, None, None), "null"),

@@ -54,6 +54,22 @@ def test_pipeline_reuses_host_buffers_and_runs_twice():
         assert torch.equal(out[1], block(b.cuda()).cpu())
 
 
+@pytest.mark.parametrize("slots", [2, 3])
+def test_graph_replayed_pipeline_matches_device_forward(slots):
+    """graphs=True replays one captured forward per slot: same bits as eager."""
+    w = WORKLOADS["small"]
+    block = make_block("small")
+    inputs = [block_input(w, first_token=i * w.tokens).pin_memory() for i in range(5)]
+    outputs = [torch.empty_like(inputs[0]).pin_memory() for _ in range(5)]
+    pipe = HostPipeline(block, w.tokens, slots=slots, graphs=True)
+    for _ in range(2):
+        pipe.run(inputs, outputs)
+        for x, got in zip(inputs, outputs):
+            assert torch.equal(got, block(x.cuda()).cpu())
+    pipe.close()
+    assert block.extension.device_status() == 0
+
+
 def test_forward_out_argument():
     w = WORKLOADS["small"]
     block = make_block("small")

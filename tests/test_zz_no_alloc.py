@@ -1,8 +1,8 @@
 """moe_dispatch_no_alloc: the dispatch entry point for callers that cannot allocate.
 
-Callers inside a CUDA graph capture, hosts that forbid device allocation after
-start-up, and bindings that hold only raw device pointers cannot provide the
-scratch buffer moe_dispatch asks for.  moe_dispatch_no_alloc uses a fixed
+Serving hosts that fix their device memory at start-up and forbid allocation
+afterwards, and language bindings that hold only raw device pointers, cannot
+provide the scratch buffer moe_dispatch asks for.  moe_dispatch_no_alloc uses a fixed
 array compiled into the library instead.  This test calls it through the C ABI
 twice in a row, with different shapes, and requires its results to equal the
 regular entry point's bit for bit -- the same tolerance as every other
