@@ -42,6 +42,11 @@ SIGNATURES = {
     "moe_grouped_gemm_swiglu": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "moe_grouped_gemm": (ctypes.c_int, [_P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "moe_grouped_gemm_tile": (ctypes.c_int32, [_I64, _I32]),
+    "moe_quantize_rows_e4m3": (ctypes.c_int, [_P, _I32, _P, _P, _I64, _I64, _P]),
+    "moe_grouped_gemm_swiglu_e4m3": (
+        ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]
+    ),
+    "moe_grouped_gemm_e4m3": (ctypes.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I32, _P]),
     "moe_ep_layout": (ctypes.c_int, [_P, _I32, _I32, _I32, _P, _P, _P, _P]),
     "moe_ep_regroup": (
         ctypes.c_int, [_P, _I32, _P, _P, _P, _P, _P, _I32, _I32, _I64, _I64, _I64, _I32, _P]
@@ -312,6 +317,58 @@ class Extension:
             a.data_ptr(), weight.data_ptr(), offsets.data_ptr(), out.data_ptr(), a.shape[0],
             n_cols, k_dim, experts,
         )
+
+    # --------------------------------------------------- FP8 (e4m3) experts
+    def quantize_rows_e4m3(self, x, q, scale):
+        """q[r] = e4m3(x[r] * 448 / amax_r), scale[r] = amax_r / 448 (include/moe_b200.h)."""
+        _require(x.is_cuda and x.is_contiguous() and x.dtype == torch.bfloat16 and x.dim() == 2,
+                 "expected contiguous BF16 CUDA x[R,C]")
+        _check_cuda(q, x, "quantize_rows_e4m3")
+        _check_cuda(scale, x, "quantize_rows_e4m3")
+        _require(q.dtype == torch.float8_e4m3fn and tuple(q.shape) == tuple(x.shape),
+                 "expected float8_e4m3fn q with x's shape")
+        _require(scale.dtype == torch.float32 and scale.numel() == x.shape[0],
+                 "expected fp32 scale[R]")
+        self._call(x.device, self.lib.moe_quantize_rows_e4m3, x.data_ptr(), 2, q.data_ptr(),
+                   scale.data_ptr(), x.shape[0], x.shape[1])
+
+    def _e4m3_checks(self, a, a_scale, weight, weight_scale, offsets, out):
+        _require(a.is_cuda and a.is_contiguous() and a.dtype == torch.float8_e4m3fn and a.dim() == 2,
+                 "expected contiguous float8_e4m3fn CUDA rows[R,K]")
+        for tensor in (a_scale, weight, weight_scale, offsets, out):
+            _check_cuda(tensor, a, "e4m3 grouped GEMM")
+        _require(weight.dim() == 3 and weight.dtype == torch.float8_e4m3fn
+                 and weight.shape[2] == a.shape[1], "expected float8_e4m3fn weight[E,N,K]")
+        _require(a_scale.dtype == torch.float32 and a_scale.numel() == a.shape[0],
+                 "expected fp32 a_scale[R]")
+        _require(weight_scale.dtype == torch.float32
+                 and weight_scale.numel() == weight.shape[0] * weight.shape[1],
+                 "expected fp32 weight_scale[E*N]")
+        _require(offsets.dtype == torch.int32 and offsets.numel() == weight.shape[0] + 1,
+                 "expected int32 offsets[E+1]")
+        _require(out.dtype == torch.bfloat16 and out.dim() == 2 and out.shape[0] == a.shape[0],
+                 "expected BF16 out[R,N]")
+
+    def grouped_gemm_swiglu_e4m3_out(self, packed_q, packed_scale, gate_up_q, gate_up_scale,
+                                     offsets, activated):
+        """Gate/up grouped GEMM on e4m3 operands with SwiGLU in its epilogue."""
+        self._e4m3_checks(packed_q, packed_scale, gate_up_q, gate_up_scale, offsets, activated)
+        experts, two_i, hidden = gate_up_q.shape
+        _require(two_i % 2 == 0 and activated.shape[1] * 2 == two_i,
+                 "expected gate_up[E,2I,H] and activated[R,I]")
+        self._call(packed_q.device, self.lib.moe_grouped_gemm_swiglu_e4m3, packed_q.data_ptr(),
+                   packed_scale.data_ptr(), gate_up_q.data_ptr(), gate_up_scale.data_ptr(),
+                   offsets.data_ptr(), activated.data_ptr(), packed_q.shape[0], hidden,
+                   two_i // 2, experts)
+
+    def grouped_gemm_e4m3_out(self, a_q, a_scale, weight_q, weight_scale, offsets, out):
+        """Plain grouped GEMM on e4m3 operands: out[r] = dequantised a[r] @ weight[e].T."""
+        self._e4m3_checks(a_q, a_scale, weight_q, weight_scale, offsets, out)
+        experts, n_cols, k_dim = weight_q.shape
+        _require(out.shape[1] == n_cols, "expected out[R,N]")
+        self._call(a_q.device, self.lib.moe_grouped_gemm_e4m3, a_q.data_ptr(), a_scale.data_ptr(),
+                   weight_q.data_ptr(), weight_scale.data_ptr(), offsets.data_ptr(), out.data_ptr(),
+                   a_q.shape[0], n_cols, k_dim, experts)
 
     # ------------------------------------------------------- expert parallel
     def ep_layout(self, counts, alignment, src_start, dst_start, offsets):

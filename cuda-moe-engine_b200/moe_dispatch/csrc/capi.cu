@@ -243,6 +243,60 @@ int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, 
     return grouped_gemm_common(a, weight, offsets, out, rows, n_cols, k_dim, experts, false, stream);
 }
 
+int moe_quantize_rows_e4m3(const void* x, int32_t dtype, void* q, float* scale, int64_t rows,
+                           int64_t cols, void* stream) {
+    if (dtype != moe::kBF16) return fail(MOE_ERR_INVALID, "e4m3 quantisation takes bf16 rows");
+    if (rows < 0 || cols < 8 || cols % 16 || rows > INT_MAX)
+        return fail(MOE_ERR_INVALID, "e4m3 rows need cols a positive multiple of 16");
+    if (rows > 0 && (!x || !q || !scale)) return fail(MOE_ERR_INVALID, "null pointer");
+    if (rows > 0 && (!aligned(x, 16) || !aligned(q, 16) || !aligned(scale, 4)))
+        return fail(MOE_ERR_INVALID, "x and q must be 16-byte aligned");
+    return cuda_status(moe::launch_quantize_rows_e4m3(x, q, scale, rows, cols,
+                                                      static_cast<cudaStream_t>(stream)),
+                       "moe_quantize_rows_e4m3");
+}
+
+static int grouped_gemm_e4m3_common(const void* a, const float* a_scale, const void* w,
+                                    const float* w_scale, const int32_t* offsets, void* out,
+                                    int64_t rows, int64_t n_out, int64_t k_dim, int32_t experts,
+                                    bool swiglu, void* stream) {
+    if (rows < 0 || rows > INT_MAX) return fail(MOE_ERR_INVALID, "rows must be in 0..INT_MAX");
+    if (n_out < 8 || n_out % 8 || k_dim < 16 || k_dim % 16)
+        return fail(MOE_ERR_INVALID,
+                    "e4m3 grouped GEMM needs n a positive multiple of 8 and k of 16");
+    if (experts < 1) return fail(MOE_ERR_INVALID, "experts must be >= 1");
+    const int64_t b_rows = (swiglu ? 2 : 1) * n_out * static_cast<int64_t>(experts);
+    if (b_rows > INT_MAX || n_out > INT_MAX / 2)
+        return fail(MOE_ERR_INVALID, "weight shape exceeds int32 coordinates");
+    if (rows > 0 && (!a || !a_scale || !w || !w_scale || !offsets || !out))
+        return fail(MOE_ERR_INVALID, "null pointer");
+    if (rows > 0 && (!aligned(a, 16) || !aligned(w, 16) || !aligned(out, 16)))
+        return fail(MOE_ERR_INVALID, "GEMM operands must be 16-byte aligned");
+    const char* message = nullptr;
+    cudaError_t err = moe::launch_grouped_gemm(a, w, offsets, out, rows, n_out, k_dim, experts,
+                                               swiglu, static_cast<cudaStream_t>(stream), &message,
+                                               a_scale, w_scale);
+    if (message) return fail(MOE_ERR_INVALID, "%s", message);
+    return cuda_status(err, swiglu ? "moe_grouped_gemm_swiglu_e4m3" : "moe_grouped_gemm_e4m3");
+}
+
+int moe_grouped_gemm_swiglu_e4m3(const void* packed_q, const float* packed_scale,
+                                 const void* gate_up_q, const float* gate_up_scale,
+                                 const int32_t* offsets, void* activated, int64_t rows,
+                                 int64_t hidden, int64_t intermediate, int32_t experts,
+                                 void* stream) {
+    return grouped_gemm_e4m3_common(packed_q, packed_scale, gate_up_q, gate_up_scale, offsets,
+                                    activated, rows, intermediate, hidden, experts, true, stream);
+}
+
+int moe_grouped_gemm_e4m3(const void* a_q, const float* a_scale, const void* weight_q,
+                          const float* weight_scale, const int32_t* offsets, void* out,
+                          int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts,
+                          void* stream) {
+    return grouped_gemm_e4m3_common(a_q, a_scale, weight_q, weight_scale, offsets, out, rows,
+                                    n_cols, k_dim, experts, false, stream);
+}
+
 int32_t moe_grouped_gemm_tile(int64_t rows, int32_t experts) {
     return moe::grouped_gemm_uses_pair(rows, experts) ? 1 : 0;
 }

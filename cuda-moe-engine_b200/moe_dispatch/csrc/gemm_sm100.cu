@@ -104,7 +104,9 @@ struct GemmParams {
     int n_tiles;         // output column tiles
     int b_rows;          // weight rows per expert (2*I for SwiGLU, N otherwise)
     int up_offset;       // row offset of the "up" half inside an expert (SwiGLU)
-    uint32_t* sched;     // this launch's {claim counter, CTAs finished}
+    uint32_t* sched;     // this launch's {claim counter, CTAs finished, CTAs entered}
+    const float* a_scale;  // e4m3 operands: dequantisation scale per A row
+    const float* b_scale;  // e4m3 operands: dequantisation scale per weight row
 };
 
 // ---------------------------------------------------------------- PTX helpers
@@ -215,11 +217,16 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
            (static_cast<uint64_t>(2) << 61);
 }
 
-// Instruction descriptor: D fp32, A and B bf16, both K-major, M x N.
-constexpr uint32_t make_idesc(int m, int n) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+// Instruction descriptor: D fp32, both operands K-major, M x N; A and B bf16
+// (format 1 for kind::f16) or e4m3 (format 0 for kind::f8f6f4).
+constexpr uint32_t make_idesc(int m, int n, bool fp8 = false) {
+    const uint32_t ab = fp8 ? 0u : ((1u << 7) | (1u << 10));
+    return (1u << 4) | ab | (static_cast<uint32_t>(n >> 3) << 17) |
            (static_cast<uint32_t>(m >> 4) << 24);
 }
+
+// Elements of one 128-byte swizzled row: one k-block per pipeline stage.
+template <bool kFp8> constexpr int stage_k() { return kFp8 ? 128 : kBK; }
 
 __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
                                           uint32_t idesc, uint32_t accumulate) {
@@ -228,6 +235,23 @@ __device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t desc_a, uint
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
         "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+// e4m3 x e4m3 -> fp32, K = 32 per instruction (32 bytes of each operand row).
+__device__ __forceinline__ void umma_e4m3(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+template <bool kFp8>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                     uint32_t idesc, uint32_t accumulate) {
+    if constexpr (kFp8) umma_e4m3(tmem_d, desc_a, desc_b, idesc, accumulate);
+    else umma_bf16(tmem_d, desc_a, desc_b, idesc, accumulate);
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -299,12 +323,13 @@ __device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int exp
     m = local - n * mt;
 }
 
-template <bool kSwiglu, bool kScatter = false>
+template <bool kSwiglu, bool kScatter = false, bool kFp8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const __grid_constant__ CUtensorMap tmap_b, const GemmParams p,
                     const GemmScatter scatter) {
     static_assert(!(kSwiglu && kScatter), "the scatter epilogue is for the down GEMM");
+    static_assert(!(kFp8 && kScatter), "the scatter epilogue takes bf16 operands");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -324,7 +349,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
-    const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+    constexpr int kStageK = stage_k<kFp8>();
+    const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
 
     // m-tiles per expert -> exclusive prefix (warp 0).
@@ -418,9 +444,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     uint8_t* sa = tiles + stage * kStageBytes;
                     uint8_t* sb = sa + kTileABytes;
                     mbar_expect_tx(&full[stage], kStageBytes);
-                    tma_load_2d(sa, &tmap_a, &full[stage], kb * kBK, row0);
-                    tma_load_2d(sb, &tmap_b, &full[stage], kb * kBK, brow);
-                    tma_load_2d(sb + kBoxBytes, &tmap_b, &full[stage], kb * kBK, brow2);
+                    tma_load_2d(sa, &tmap_a, &full[stage], kb * kStageK, row0);
+                    tma_load_2d(sb, &tmap_b, &full[stage], kb * kStageK, brow);
+                    tma_load_2d(sb + kBoxBytes, &tmap_b, &full[stage], kb * kStageK, brow2);
                     armed |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == kStages) {
@@ -442,7 +468,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else if (warp == 1) {
         if (lane == 0) {
             // ------------------------------------------------ MMA issuer
-            constexpr uint32_t idesc = make_idesc(kBM, kBN);
+            constexpr uint32_t idesc = make_idesc(kBM, kBN, kFp8);
             int stage = 0;
             uint32_t phase = 0;
             int ring = 0;
@@ -473,7 +499,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const uint32_t b_addr = a_addr + kTileABytes;
 #pragma unroll
                     for (int k = 0; k < kBK / kUmmaK; ++k)
-                        umma_bf16(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
+                        umma<kFp8>(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
                                   smem_desc_sw128(b_addr + k * kUmmaK * 2), idesc,
                                   (kb | k) != 0 ? 1u : 0u);
                     issued = true;
@@ -518,6 +544,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
+            // e4m3: out = bf16((acc * row scale) * column scale); the row scale is
+            // read once per tile, the column scales once per 32-column chunk
+            float rscale = 1.0f, gscale = 1.0f, uscale = 1.0f;
+            if constexpr (kFp8) rscale = valid ? __ldg(p.a_scale + row) : 0.0f;
             if constexpr (kScatter) {
                 // the source rank and packed row this grouped row returns to
                 valid = false;
@@ -543,24 +573,47 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     uint32_t u[32];
                     tmem_ld32(taddr + c, v);
                     tmem_ld32(taddr + kBN / 2 + c, u);
+                    if constexpr (kFp8) {
+                        // lane l holds the scales of column col0 + l (gate and up rows)
+                        const int col = n * kOutTile + c + lane;
+                        const bool in = col < p.n_out;
+                        gscale = in ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + col) : 0.0f;
+                        uscale = in ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + p.up_offset + col) : 0.0f;
+                    }
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         float a2[2];
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
-                            const float g = round_bf16(__uint_as_float(v[2 * j + h]));
-                            const float up = round_bf16(__uint_as_float(u[2 * j + h]));
+                            float gv = __uint_as_float(v[2 * j + h]);
+                            float uv = __uint_as_float(u[2 * j + h]);
+                            if constexpr (kFp8) {
+                                gv = (gv * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j + h);
+                                uv = (uv * rscale) * __shfl_sync(0xffffffffu, uscale, 2 * j + h);
+                            }
+                            const float g = round_bf16(gv);
+                            const float up = round_bf16(uv);
                             a2[h] = (g / (1.0f + expf(-g))) * up;
                         }
                         outw[j] = pack_bf16x2(a2[0], a2[1]);
                     }
                 } else {
                     tmem_ld32(taddr + c, v);
+                    if constexpr (kFp8) {
+                        const int col = n * kOutTile + c + lane;
+                        gscale = col < p.n_out ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + col) : 0.0f;
+                    }
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        outw[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                    for (int j = 0; j < 16; ++j) {
+                        float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
+                        if constexpr (kFp8) {
+                            lo = (lo * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j);
+                            hi = (hi * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j + 1);
+                        }
+                        outw[j] = pack_bf16x2(lo, hi);
+                    }
                 }
                 if (valid) {
                     const int col0 = n * kOutTile + c;
@@ -670,6 +723,22 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t desc_a,
         "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
 }
 
+__device__ __forceinline__ void umma_e4m3_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                               uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate));
+}
+
+template <bool kFp8>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b,
+                                          uint32_t idesc, uint32_t accumulate) {
+    if constexpr (kFp8) umma_e4m3_pair(tmem_d, desc_a, desc_b, idesc, accumulate);
+    else umma_bf16_pair(tmem_d, desc_a, desc_b, idesc, accumulate);
+}
+
 // Arrives (once) on the barrier at this shared offset in both CTAs of the pair
 // when every tcgen05 operation issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
@@ -679,7 +748,7 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
-template <bool kSwiglu>
+template <bool kSwiglu, bool kFp8 = false>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                          const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
@@ -704,7 +773,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
     const bool leader = rank == 0;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
-    const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+    constexpr int kStageK = stage_k<kFp8>();
+    const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
 
     // m-tiles (256 rows) per expert -> exclusive prefix (warp 0, both CTAs).
@@ -807,8 +877,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const uint32_t leader_full = map_to_cta(smem_u32(&full[stage]), 0);
                     uint8_t* sa = tiles + stage * kPairStageBytes;
                     if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
-                    tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kBK, row0);
-                    tma_load_2d_pair(sa + kPairTileABytes, &tmap_b, leader_full, kb * kBK, brow);
+                    tma_load_2d_pair(sa, &tmap_a, leader_full, kb * kStageK, row0);
+                    tma_load_2d_pair(sa + kPairTileABytes, &tmap_b, leader_full, kb * kStageK, brow);
                     armed |= 1u << stage;
                     last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
                     if (++stage == kPairStages) {
@@ -829,7 +899,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     } else if (warp == 1) {
         if (lane == 0 && leader) {
             // ------------------------------------------------ MMA issuer (leader only)
-            constexpr uint32_t idesc = make_idesc(kPairBM, kBN);
+            constexpr uint32_t idesc = make_idesc(kPairBM, kBN, kFp8);
             int stage = 0;
             uint32_t phase = 0;
             int ring = 0;
@@ -860,7 +930,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     const uint32_t b_addr = a_addr + kPairTileABytes;
 #pragma unroll
                     for (int k = 0; k < kBK / kUmmaK; ++k)
-                        umma_bf16_pair(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
+                        umma_pair<kFp8>(d, smem_desc_sw128(a_addr + k * kUmmaK * 2),
                                        smem_desc_sw128(b_addr + k * kUmmaK * 2), idesc,
                                        (kb | k) != 0 ? 1u : 0u);
                     issued = true;
@@ -907,6 +977,10 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             const bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
+            // e4m3: out = bf16((acc * row scale) * column scale); the row scale is
+            // read once per tile, the column scales once per 32-column chunk
+            float rscale = 1.0f, gscale = 1.0f, uscale = 1.0f;
+            if constexpr (kFp8) rscale = valid ? __ldg(p.a_scale + row) : 0.0f;
 #pragma unroll 1
             for (int c = group * (kOutTile / kEpilogueGroups); c < (group + 1) * (kOutTile / kEpilogueGroups);
                  c += 32) {
@@ -916,24 +990,47 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                     uint32_t u[32];
                     tmem_ld32(taddr + c, v);
                     tmem_ld32(taddr + kBN / 2 + c, u);
+                    if constexpr (kFp8) {
+                        // lane l holds the scales of column col0 + l (gate and up rows)
+                        const int col = n * kOutTile + c + lane;
+                        const bool in = col < p.n_out;
+                        gscale = in ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + col) : 0.0f;
+                        uscale = in ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + p.up_offset + col) : 0.0f;
+                    }
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         float a2[2];
 #pragma unroll
                         for (int h = 0; h < 2; ++h) {
-                            const float g = round_bf16(__uint_as_float(v[2 * j + h]));
-                            const float up = round_bf16(__uint_as_float(u[2 * j + h]));
+                            float gv = __uint_as_float(v[2 * j + h]);
+                            float uv = __uint_as_float(u[2 * j + h]);
+                            if constexpr (kFp8) {
+                                gv = (gv * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j + h);
+                                uv = (uv * rscale) * __shfl_sync(0xffffffffu, uscale, 2 * j + h);
+                            }
+                            const float g = round_bf16(gv);
+                            const float up = round_bf16(uv);
                             a2[h] = (g / (1.0f + expf(-g))) * up;
                         }
                         outw[j] = pack_bf16x2(a2[0], a2[1]);
                     }
                 } else {
                     tmem_ld32(taddr + c, v);
+                    if constexpr (kFp8) {
+                        const int col = n * kOutTile + c + lane;
+                        gscale = col < p.n_out ? __ldg(p.b_scale + static_cast<int64_t>(e) * p.b_rows + col) : 0.0f;
+                    }
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        outw[j] = pack_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+                    for (int j = 0; j < 16; ++j) {
+                        float lo = __uint_as_float(v[2 * j]), hi = __uint_as_float(v[2 * j + 1]);
+                        if constexpr (kFp8) {
+                            lo = (lo * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j);
+                            hi = (hi * rscale) * __shfl_sync(0xffffffffu, gscale, 2 * j + 1);
+                        }
+                        outw[j] = pack_bf16x2(lo, hi);
+                    }
                 }
                 if (valid) {
                     const int col0 = n * kOutTile + c;
@@ -976,17 +1073,20 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
-// Row-major bf16 matrix [rows, cols], boxes of box_rows rows x 64 columns, 128B swizzle.
+// Row-major matrix [rows, cols] of bf16 (or e4m3 bytes with fp8), boxes of
+// box_rows rows x 128 bytes, 128B swizzle.
 bool make_tensor_map(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols,
-                     uint32_t box_rows = kBoxRows) {
+                     bool fp8 = false, uint32_t box_rows = kBoxRows) {
     auto encode = tensor_map_encoder();
     if (!encode) return false;
+    const uint64_t elem = fp8 ? 1 : 2;
     cuuint64_t dims[2] = {cols, rows};
-    cuuint64_t strides[1] = {cols * 2};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(kBK), static_cast<cuuint32_t>(box_rows)};
+    cuuint64_t strides[1] = {cols * elem};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / elem), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t elem_strides[2] = {1, 1};
-    return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+    return encode(map, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, elem_strides,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -995,8 +1095,8 @@ struct DeviceInfo {
     int sms = 0;
     int pair_clusters = 0;
     uint32_t* sched = nullptr;  // device address of g_tile_sched
-    bool configured[2] = {false, false};
-    bool pair_configured[2] = {false, false};
+    bool configured[2][2] = {};       // [fp8][swiglu]
+    bool pair_configured[2][2] = {};  // [fp8][swiglu]
 };
 
 DeviceInfo& device_info(int device) {
@@ -1075,7 +1175,9 @@ cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& re
 
 cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
                                 int64_t rows, int64_t n_out, int64_t k_dim, int experts,
-                                bool swiglu, cudaStream_t stream, const char** error) {
+                                bool swiglu, cudaStream_t stream, const char** error,
+                                const float* a_scale, const float* b_scale) {
+    const bool fp8 = a_scale != nullptr;
     *error = nullptr;
     if (rows == 0 || experts == 0) return cudaSuccess;
     if (experts > kMaxExperts) {
@@ -1088,12 +1190,14 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     if (info.sms == 0) MOE_CUDA_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
     const int64_t b_rows = swiglu ? 2 * n_out : n_out;
     CUtensorMap map_a, map_b;
-    if (!make_tensor_map(&map_a, a, static_cast<uint64_t>(rows), static_cast<uint64_t>(k_dim)) ||
-        !make_tensor_map(&map_b, b, static_cast<uint64_t>(b_rows * experts), static_cast<uint64_t>(k_dim))) {
+    if (!make_tensor_map(&map_a, a, static_cast<uint64_t>(rows), static_cast<uint64_t>(k_dim), fp8) ||
+        !make_tensor_map(&map_b, b, static_cast<uint64_t>(b_rows * experts), static_cast<uint64_t>(k_dim), fp8)) {
         *error = "cuTensorMapEncodeTiled rejected an operand (pointer alignment or shape)";
         return cudaErrorInvalidValue;
     }
     GemmParams p;
+    p.a_scale = a_scale;
+    p.b_scale = b_scale;
     p.offsets = offsets;
     p.out = static_cast<__nv_bfloat16*>(out);
     p.ldo = n_out;
@@ -1110,14 +1214,16 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     if (tile == Tile::kPair) {
         const int64_t max_tiles =
             ((rows + kPairBM - 1) / kPairBM + experts) * static_cast<int64_t>(p.n_tiles);
-        return launch_pair(swiglu ? grouped_gemm_pair_kernel<true> : grouped_gemm_pair_kernel<false>,
-                           kPairSmemBytes, info.pair_configured[swiglu], info.pair_clusters,
+        auto pair = fp8 ? (swiglu ? grouped_gemm_pair_kernel<true, true> : grouped_gemm_pair_kernel<false, true>)
+                        : (swiglu ? grouped_gemm_pair_kernel<true, false> : grouped_gemm_pair_kernel<false, false>);
+        return launch_pair(pair, kPairSmemBytes, info.pair_configured[fp8][swiglu], info.pair_clusters,
                            info.sms, max_tiles, map_a, map_b, p, stream);
     }
-    auto kernel = swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>;
-    if (!info.configured[swiglu]) {
+    auto kernel = fp8 ? (swiglu ? grouped_gemm_kernel<true, false, true> : grouped_gemm_kernel<false, false, true>)
+                      : (swiglu ? grouped_gemm_kernel<true> : grouped_gemm_kernel<false>);
+    if (!info.configured[fp8][swiglu]) {
         MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-        info.configured[swiglu] = true;
+        info.configured[fp8][swiglu] = true;
     }
     const int64_t max_tiles = ((rows + kBM - 1) / kBM + experts) * static_cast<int64_t>(p.n_tiles);
     const int grid = static_cast<int>(max_tiles < info.sms ? max_tiles : info.sms);
@@ -1162,6 +1268,7 @@ cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int3
     p.n_tiles = static_cast<int>((n_out + kBN - 1) / kBN);
     p.b_rows = static_cast<int>(n_out);
     p.up_offset = 0;
+    p.a_scale = p.b_scale = nullptr;
     MOE_CUDA_TRY(schedule_slot(info, stream, &p.sched));
     // every CTA takes part in the completion ticket, so the grid never depends on the rows
     kernel<<<info.sms, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, scatter);

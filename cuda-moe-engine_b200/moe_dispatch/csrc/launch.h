@@ -37,9 +37,16 @@ cudaError_t launch_swiglu(const void* projection, int dtype, const int32_t* vali
 
 // Grouped GEMMs on tcgen05 (gemm_sm100.cu).  `error` receives a message when
 // the returned status is not cudaSuccess because of a host-side check.
+// With a_scale (and b_scale) non-null, a and b are e4m3 bytes and every
+// accumulator is dequantised as (acc * a_scale[row]) * b_scale[weight row].
 cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
                                 int64_t rows, int64_t n_out, int64_t k_dim, int experts,
-                                bool swiglu, cudaStream_t stream, const char** error);
+                                bool swiglu, cudaStream_t stream, const char** error,
+                                const float* a_scale = nullptr, const float* b_scale = nullptr);
+// e4m3 quantisation of bf16 rows: scale[r] = amax_r / 448, q[r,c] = e4m3(x[r,c] * (448 / amax_r))
+// (round to nearest even, saturating); an all-zero row gets scale 1 and zeros.
+cudaError_t launch_quantize_rows_e4m3(const void* x, void* q, float* scale, int64_t rows,
+                                      int64_t cols, cudaStream_t stream);
 cudaError_t read_gemm_status(int32_t* code, bool clear);
 cudaError_t read_route_status(int32_t* code, bool clear);
 bool grouped_gemm_uses_pair(int64_t rows, int experts);

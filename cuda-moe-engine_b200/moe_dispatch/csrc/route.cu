@@ -18,6 +18,8 @@
 #include "launch.h"
 
 #include <climits>
+#include <cstdlib>
+#include <cstring>
 
 namespace moe {
 
@@ -35,71 +37,125 @@ cudaError_t read_route_status(int32_t* code, bool clear) {
 
 namespace {
 
-// Many experts (E > 32): 128-token x TE-expert tiles, 256 threads, an MT x ME
-// register micro-tile per thread, hidden consumed in chunks of 16 staged in
-// two shared-memory buffers (the next chunk's global loads are in flight while
-// the current one is used).  Every logit is still one sequential FMA chain in
-// increasing h, so the tiling does not change any value.
-template <int TE, int ME>
-__global__ void __launch_bounds__(256)
+// Many experts (E > 32): TT-token x TE-expert tiles, (TT/MT)*(TE/ME) threads,
+// an MT x ME register micro-tile per thread, hidden consumed in chunks of KC
+// staged in two shared-memory buffers (the next chunk's global loads are in
+// flight while the current one is used).  Every logit is still one sequential
+// FMA chain in increasing h: the packed __ffma2_rn does two independent fp32
+// FMAs (round to nearest, like fmaf), pairing neighbouring experts, so the
+// tiling and pairing change no value.  The transposing stores into shared
+// memory give consecutive lanes consecutive tokens (experts), so they are
+// free of bank conflicts.
+template <int TT, int TE, int MT, int ME>
+struct TiledRouter {
+    static constexpr int KC = 32;
+    static constexpr int kThreads = (TT / MT) * (TE / ME);
+    static constexpr int kTx = TE / ME;                    // threads along experts
+    static constexpr int kXPieces = TT * (KC / 8) / kThreads;   // 16-byte x pieces per thread
+    static constexpr int kWPieces = TE * (KC / 4) / kThreads;   // 16-byte w pieces per thread
+    static constexpr int kSmemBytes = 2 * KC * (TT + TE) * 4;
+    static_assert(kXPieces * kThreads == TT * (KC / 8), "x pieces split evenly");
+    static_assert(kWPieces * kThreads == TE * (KC / 4), "w pieces split evenly");
+    static_assert(MT % 4 == 0 && ME % 4 == 0, "float4 micro-tile loads");
+};
+
+template <int TT, int TE, int MT, int ME>
+__global__ void __launch_bounds__(TiledRouter<TT, TE, MT, ME>::kThreads, 2)
 router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                            float* __restrict__ logits, int64_t tokens, int hidden, int experts) {
-    constexpr int TT = 128, MT = 8, KC = 16;
-    constexpr int kTx = TE / ME;  // threads along experts
-    static_assert((TT / MT) * kTx == 256, "256 threads");
-    __shared__ __align__(16) float xs[2][KC][TT];
-    __shared__ __align__(16) float ws[2][KC][TE];
+    using R = TiledRouter<TT, TE, MT, ME>;
+    constexpr int KC = R::KC, NT = R::kThreads;
+    extern __shared__ __align__(16) float router_smem[];
+    float* xs = router_smem;                 // [2][KC][TT]
+    float* ws = router_smem + 2 * KC * TT;   // [2][KC][TE]
     const int tid = threadIdx.x;
-    const int tx = tid % kTx, ty = tid / kTx;
+    const int tx = tid % R::kTx, ty = tid / R::kTx;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
     const int e0 = blockIdx.y * TE;
 
-    // global -> register staging: x 128 rows x 16 h (bf16) = one 16-byte piece per
-    // thread; W TE rows x 16 h (fp32) = TE*4 16-byte pieces.
-    constexpr int kWPieces = TE * KC / 4 / 256;
-    uint4 xr;
-    float4 wr[kWPieces];
+    uint4 xr[R::kXPieces];
+    float4 wr[R::kWPieces];
     auto load = [&](int h0) {
-        const int row = tid >> 1, half = tid & 1;
-        const int64_t t = t0 + row;
-        const int h = h0 + half * 8;
-        xr = make_uint4(0, 0, 0, 0);
-        if (t < tokens && h < hidden) xr = __ldg(reinterpret_cast<const uint4*>(x + t * hidden + h));
 #pragma unroll
-        for (int q = 0; q < kWPieces; ++q) {
-            const int v = tid + q * 256;
-            const int er = v >> 2, piece = v & 3;
+        for (int q = 0; q < R::kXPieces; ++q) {
+            const int piece = tid + q * NT;
+            const int row = piece % TT, part = piece / TT;
+            const int64_t t = t0 + row;
+            const int h = h0 + part * 8;
+            xr[q] = make_uint4(0, 0, 0, 0);
+            if (t < tokens && h < hidden) xr[q] = __ldg(reinterpret_cast<const uint4*>(x + t * hidden + h));
+        }
+#pragma unroll
+        for (int q = 0; q < R::kWPieces; ++q) {
+            const int piece = tid + q * NT;
+            const int er = piece % TE, part = piece / TE;
             const int e = e0 + er;
-            const int hh = h0 + piece * 4;
+            const int h = h0 + part * 4;
             wr[q] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (e < experts && hh < hidden)
-                wr[q] = __ldg(reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + hh));
+            if (e < experts && h < hidden)
+                wr[q] = __ldg(reinterpret_cast<const float4*>(w + static_cast<int64_t>(e) * hidden + h));
         }
     };
     auto store = [&](int buf) {
-        const int row = tid >> 1, half = tid & 1;
-        const uint32_t words[4] = {xr.x, xr.y, xr.z, xr.w};
+        float* xb = xs + buf * KC * TT;
+        float* wb = ws + buf * KC * TE;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            xs[buf][half * 8 + 2 * q][row] = bf16_bits_to_f32(words[q] & 0xffffu);
-            xs[buf][half * 8 + 2 * q + 1][row] = bf16_bits_to_f32(words[q] >> 16);
+        for (int q = 0; q < R::kXPieces; ++q) {
+            const int piece = tid + q * NT;
+            const int row = piece % TT, part = piece / TT;
+            const uint32_t words[4] = {xr[q].x, xr[q].y, xr[q].z, xr[q].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                xb[(part * 8 + 2 * j) * TT + row] = bf16_bits_to_f32(words[j] & 0xffffu);
+                xb[(part * 8 + 2 * j + 1) * TT + row] = bf16_bits_to_f32(words[j] >> 16);
+            }
         }
 #pragma unroll
-        for (int q = 0; q < kWPieces; ++q) {
-            const int v = tid + q * 256;
-            const int er = v >> 2, piece = v & 3;
-            ws[buf][piece * 4 + 0][er] = wr[q].x;
-            ws[buf][piece * 4 + 1][er] = wr[q].y;
-            ws[buf][piece * 4 + 2][er] = wr[q].z;
-            ws[buf][piece * 4 + 3][er] = wr[q].w;
+        for (int q = 0; q < R::kWPieces; ++q) {
+            const int piece = tid + q * NT;
+            const int er = piece % TE, part = piece / TE;
+            wb[(part * 4 + 0) * TE + er] = wr[q].x;
+            wb[(part * 4 + 1) * TE + er] = wr[q].y;
+            wb[(part * 4 + 2) * TE + er] = wr[q].z;
+            wb[(part * 4 + 3) * TE + er] = wr[q].w;
         }
     };
 
-    float acc[MT][ME];
+    // Thread (tx, ty) owns tokens ty*MH + i and TT/2 + ty*MH + i (i < MH), and
+    // experts tx*NH + j and TE/2 + tx*NH + j (j < NH): each quarter-warp's
+    // shared-memory reads of one half are contiguous, so they are free of bank
+    // conflicts (a contiguous MT x ME block per thread strides them 2-way).
+    constexpr int MH = MT / 2, NH = ME / 2;
+    static_assert(MH == 4 && (NH == 4 || NH == 2), "micro-tile halves of 4 tokens, 2 or 4 experts");
+    float2 acc[MT][NH];
 #pragma unroll
     for (int i = 0; i < MT; ++i)
 #pragma unroll
-        for (int j = 0; j < ME; ++j) acc[i][j] = 0.0f;
+        for (int j = 0; j < NH; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
+
+    auto step = [&](const float* xk, const float* wk) {
+        float xv[MT];
+        float2 wv[NH];
+        const float4 x0 = *reinterpret_cast<const float4*>(xk + ty * MH);
+        const float4 x1 = *reinterpret_cast<const float4*>(xk + TT / 2 + ty * MH);
+        xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
+        xv[4] = x1.x; xv[5] = x1.y; xv[6] = x1.z; xv[7] = x1.w;
+        if constexpr (NH == 4) {
+            const float4 w0 = *reinterpret_cast<const float4*>(wk + tx * NH);
+            const float4 w1 = *reinterpret_cast<const float4*>(wk + TE / 2 + tx * NH);
+            wv[0] = make_float2(w0.x, w0.y); wv[1] = make_float2(w0.z, w0.w);
+            wv[2] = make_float2(w1.x, w1.y); wv[3] = make_float2(w1.z, w1.w);
+        } else {
+            wv[0] = *reinterpret_cast<const float2*>(wk + tx * NH);
+            wv[1] = *reinterpret_cast<const float2*>(wk + TE / 2 + tx * NH);
+        }
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+            const float2 xx = make_float2(xv[i], xv[i]);
+#pragma unroll
+            for (int j = 0; j < NH; ++j) acc[i][j] = __ffma2_rn(xx, wv[j], acc[i][j]);
+        }
+    };
 
     load(0);
     int buf = 0;
@@ -107,38 +163,54 @@ router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
         store(buf);
         __syncthreads();
         if (h0 + KC < hidden) load(h0 + KC);
+        const float* xb = xs + buf * KC * TT;
+        const float* wb = ws + buf * KC * TE;
         const int steps = min(KC, hidden - h0);
-        for (int k = 0; k < steps; ++k) {
-            float xv[MT], wv[ME];
-            const float4* xp = reinterpret_cast<const float4*>(&xs[buf][k][ty * MT]);
-            const float4* wp = reinterpret_cast<const float4*>(&ws[buf][k][tx * ME]);
-#pragma unroll
-            for (int q = 0; q < MT / 4; ++q) {
-                const float4 v = xp[q];
-                xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
-            }
-#pragma unroll
-            for (int q = 0; q < ME / 4; ++q) {
-                const float4 v = wp[q];
-                wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
-            }
-#pragma unroll
-            for (int i = 0; i < MT; ++i)
-#pragma unroll
-                for (int j = 0; j < ME; ++j) acc[i][j] = fmaf(xv[i], wv[j], acc[i][j]);
+        if (steps == KC) {
+#pragma unroll 8
+            for (int k = 0; k < KC; ++k) step(xb + k * TT, wb + k * TE);
+        } else {
+            for (int k = 0; k < steps; ++k) step(xb + k * TT, wb + k * TE);
         }
         buf ^= 1;
     }
+    const bool vector_ok = (experts % 2) == 0;
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-        const int64_t t = t0 + ty * MT + i;
+        const int64_t t = t0 + (i < MH ? ty * MH + i : TT / 2 + ty * MH + (i - MH));
         if (t >= tokens) continue;
+        float* row = logits + t * experts;
 #pragma unroll
-        for (int j = 0; j < ME; ++j) {
-            const int e = e0 + tx * ME + j;
-            if (e < experts) logits[t * experts + e] = acc[i][j];
+        for (int j = 0; j < NH; ++j) {
+            // pair j holds experts e, e + 1 of one half
+            const int half = j / (NH / 2), jj = j % (NH / 2);
+            const int e = e0 + half * (TE / 2) + tx * NH + 2 * jj;
+            if (vector_ok && e + 2 <= experts) {
+                *reinterpret_cast<float2*>(row + e) = acc[i][j];
+            } else {
+                if (e < experts) row[e] = acc[i][j].x;
+                if (e + 1 < experts) row[e + 1] = acc[i][j].y;
+            }
         }
     }
+}
+
+template <int TT, int TE, int MT, int ME>
+cudaError_t launch_tiled(const __nv_bfloat16* x, const float* w, float* logits, int64_t tokens,
+                         int hidden, int experts, cudaStream_t stream) {
+    using R = TiledRouter<TT, TE, MT, ME>;
+    static bool configured[64] = {};
+    int device = 0;
+    MOE_CUDA_TRY(cudaGetDevice(&device));
+    if (!configured[device & 63]) {
+        MOE_CUDA_TRY(cudaFuncSetAttribute(router_logits_tiled_kernel<TT, TE, MT, ME>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, R::kSmemBytes));
+        configured[device & 63] = true;
+    }
+    dim3 grid(static_cast<unsigned>((tokens + TT - 1) / TT), static_cast<unsigned>((experts + TE - 1) / TE));
+    router_logits_tiled_kernel<TT, TE, MT, ME><<<grid, R::kThreads, R::kSmemBytes, stream>>>(
+        x, w, logits, tokens, hidden, experts);
+    return cudaGetLastError();
 }
 
 // K rounds of warp argmax over one value per lane (lane = expert, E <= 32),
@@ -480,17 +552,18 @@ cudaError_t launch_router_logits(const void* x, const float* w, float* logits, i
                                  int64_t hidden, int experts, cudaStream_t stream) {
     if (tokens == 0) return cudaSuccess;
     const auto* xb = static_cast<const __nv_bfloat16*>(x);
-    const unsigned token_tiles = static_cast<unsigned>((tokens + 127) / 128);
-    if (experts <= 64) {
-        dim3 grid(token_tiles, (experts + 63) / 64);
-        router_logits_tiled_kernel<64, 4><<<grid, 256, 0, stream>>>(xb, w, logits, tokens,
-                                                                    static_cast<int>(hidden), experts);
-    } else {
-        dim3 grid(token_tiles, (experts + 127) / 128);
-        router_logits_tiled_kernel<128, 8><<<grid, 256, 0, stream>>>(xb, w, logits, tokens,
-                                                                     static_cast<int>(hidden), experts);
-    }
-    return cudaGetLastError();
+    const int h = static_cast<int>(hidden);
+    // Tile (tokens x experts) per CTA; MOE_B200_ROUTER_TILE overrides the
+    // choice (a tuning knob: every tile gives the same bits).  Measured on B200:
+    // E=256, H=7168, T=32768: 64x128 2.88 ms, 128x128 3.14, 128x64 3.31, 64x64
+    // 3.59; E=64, H=2048, T=16384: 128x64 0.187 ms, 64x64 0.198, 32x64 0.229.
+    const char* env = getenv("MOE_B200_ROUTER_TILE");
+    const char* pick = env ? env : (experts <= 64 ? "128x64" : "64x128");
+    if (strcmp(pick, "128x128") == 0) return launch_tiled<128, 128, 8, 8>(xb, w, logits, tokens, h, experts, stream);
+    if (strcmp(pick, "64x128") == 0) return launch_tiled<64, 128, 8, 8>(xb, w, logits, tokens, h, experts, stream);
+    if (strcmp(pick, "128x64") == 0) return launch_tiled<128, 64, 8, 4>(xb, w, logits, tokens, h, experts, stream);
+    if (strcmp(pick, "32x64") == 0) return launch_tiled<32, 64, 8, 4>(xb, w, logits, tokens, h, experts, stream);
+    return launch_tiled<64, 64, 8, 4>(xb, w, logits, tokens, h, experts, stream);
 }
 
 template <int EMAX, int TW, int JC, int STAGES>

@@ -10,7 +10,11 @@ to 32).  Every stage runs a kernel from libmoe_b200.so:
   dispatch         moe_dispatch: histogram/scan/pack, aligned spans
   experts_forward  cuda_fused: tcgen05 gate/up GEMM with SwiGLU epilogue,
                    then the tcgen05 down GEMM;
-                   cuda: plain gate/up GEMM, swiglu kernel, down GEMM
+                   cuda: plain gate/up GEMM, swiglu kernel, down GEMM;
+                   expert_dtype="fp8_e4m3" (an extension: the reference's
+                   experts are bf16 only): per-row e4m3 activations and
+                   per-channel e4m3 gate/up weights on tcgen05.kind::f8f6f4,
+                   dequantised in the epilogue; the down GEMM stays bf16
   combine          moe_combine
 """
 
@@ -87,6 +91,8 @@ class LayerWorkspace:
     projection: torch.Tensor
     activated: torch.Tensor
     expert_output: torch.Tensor
+    packed_q: torch.Tensor = None      # e4m3 copy of the packed rows (expert_dtype="fp8_e4m3")
+    packed_scale: torch.Tensor = None  # their per-row dequantisation scales
 
 
 def check_out(out, x):
@@ -99,12 +105,15 @@ def check_out(out, x):
 
 
 class MoEBlock(torch.nn.Module):
-    """Inference-only top-k MoE: router, dispatch, two grouped GEMMs with SwiGLU, combine.
+    """A forward-only mixture-of-experts feed-forward layer on the B200 kernels.
 
-    `cuda_fused` fuses SwiGLU into the gate/up GEMM epilogue; `cuda` materialises
-    the bf16 projection and runs the standalone SwiGLU kernel.  Both round at the
-    same points, so they produce the same bits.  Output is a reusable view:
-    clone it before the next call.
+    Each forward routes every token to its top-k experts, packs the rows by
+    expert, runs the gate/up and down grouped GEMMs (SwiGLU between them) and
+    sums each token's expert rows weighted by its routing weights.
+    `cuda_fused` applies SwiGLU in the gate/up GEMM's epilogue; `cuda` writes
+    the bf16 projection and runs the standalone SwiGLU kernel.  Both round at
+    the same points, so they produce the same bits.  Without `out=` the result
+    lives in a buffer the next forward of the same shape reuses.
     """
 
     def __init__(
@@ -117,9 +126,15 @@ class MoEBlock(torch.nn.Module):
         expert_backend="auto",
         seed=42,
         weights=None,
+        expert_dtype="bf16",
     ):
         super().__init__()
         self.config = config or MoEConfig()
+        if expert_dtype not in ("bf16", "fp8_e4m3"):
+            raise ValueError("expert_dtype must be bf16 or fp8_e4m3")
+        if expert_dtype == "fp8_e4m3" and self.config.hidden % 16:
+            raise ValueError("fp8_e4m3 experts need hidden to be a multiple of 16")
+        self.expert_dtype = expert_dtype
         if implementation == "torch":
             raise ValueError(
                 "this engine has CUDA implementations only (cuda, cuda_fused); the PyTorch "
@@ -150,6 +165,16 @@ class MoEBlock(torch.nn.Module):
         self._workspaces = {}
         self._route_buffers = {}
         self.extension = get_extension()
+        if expert_dtype == "fp8_e4m3":
+            # gate/up weights in e4m3 with one scale per output channel (weight row);
+            # the down GEMM stays bf16
+            rows = self.gate_up_weight.shape[0] * self.gate_up_weight.shape[1]
+            q = torch.empty(self.gate_up_weight.shape, dtype=torch.float8_e4m3fn, device=device)
+            scale = torch.empty(rows, dtype=torch.float32, device=device)
+            self.extension.quantize_rows_e4m3(
+                self.gate_up_weight.view(rows, -1), q.view(rows, -1), scale)
+            self.register_buffer("gate_up_q", q)
+            self.register_buffer("gate_up_scale", scale)
 
     def set_routing_pattern(self, pattern):
         if pattern not in ("balanced", "skewed"):
@@ -189,18 +214,33 @@ class MoEBlock(torch.nn.Module):
             )
             rows = transport.capacity_rows
             projection_rows = rows if self.implementation == "cuda" else 0
+            fp8 = self.expert_dtype == "fp8_e4m3"
             self._workspaces[key] = LayerWorkspace(
                 transport,
                 torch.empty((projection_rows, 2 * cfg.intermediate), device=x.device, dtype=x.dtype),
                 torch.empty((rows, cfg.intermediate), device=x.device, dtype=x.dtype),
                 torch.empty((rows, cfg.hidden), device=x.device, dtype=x.dtype),
+                torch.empty((rows, cfg.hidden), device=x.device, dtype=torch.float8_e4m3fn)
+                if fp8 else None,
+                torch.empty(rows, device=x.device, dtype=torch.float32) if fp8 else None,
             )
         return self._workspaces[key]
 
     def experts_forward(self, state):
         transport = state.transport
         ext = self.extension
-        if self.implementation == "cuda_fused":
+        if self.expert_dtype == "fp8_e4m3":
+            # per-row e4m3 activations, e4m3 gate/up GEMM dequantised in its epilogue
+            ext.quantize_rows_e4m3(transport.packed, state.packed_q, state.packed_scale)
+            if self.implementation == "cuda_fused":
+                ext.grouped_gemm_swiglu_e4m3_out(state.packed_q, state.packed_scale, self.gate_up_q,
+                                                 self.gate_up_scale, transport.offsets,
+                                                 state.activated)
+            else:
+                ext.grouped_gemm_e4m3_out(state.packed_q, state.packed_scale, self.gate_up_q,
+                                          self.gate_up_scale, transport.offsets, state.projection)
+                ext.swiglu_out(state.projection, transport.offsets[-1:], state.activated)
+        elif self.implementation == "cuda_fused":
             ext.grouped_gemm_swiglu_out(
                 transport.packed, self.gate_up_weight, transport.offsets, state.activated
             )

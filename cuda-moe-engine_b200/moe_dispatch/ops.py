@@ -1,6 +1,7 @@
-"""Convenience API with input validation (reference: src/moe_dispatch/ops.py).
+"""Checked one-call transport functions (reference: src/moe_dispatch/ops.py).
 
-Benchmarks and the block use prevalidated workspace methods instead.
+Each call validates its tensors before launching; the block and the
+benchmarks skip that cost by calling a workspace's methods directly.
 """
 
 from dataclasses import dataclass
@@ -10,7 +11,9 @@ from .workspace import CudaWorkspace, MAX_EXPERTS, MAX_TOPK
 
 @dataclass(frozen=True)
 class PackedTokens:
-    """Views into a workspace. Clone tensors before reusing that workspace if retaining them."""
+    """The dispatch results, as tensors that alias the workspace's buffers: the
+    next dispatch into the same workspace overwrites them, so clone what must
+    outlive it."""
 
     packed: torch.Tensor
     inverse: torch.Tensor
@@ -79,7 +82,9 @@ def dispatch(x, expert_ids, experts, *, workspace=None, vectorized=True, alignme
 
 @torch.inference_mode()
 def combine(expert_output, batch, weights):
-    """Weighted gather/reduction; returns a reusable output view and accumulates in FP32."""
+    """out[t] = sum over k of weights[t,k] * expert_output[inverse[t,k]], summed in
+    fp32 and cast once; the result is the workspace's output buffer, which the
+    next combine overwrites."""
     if weights.shape != batch.inverse.shape:
         raise ValueError("weights must have shape [T,K]")
     if expert_output.shape != batch.packed.shape or expert_output.dtype != batch.packed.dtype:

@@ -77,7 +77,8 @@ class CudaWorkspace:
             self.scratch = self.extension.make_scratch(tokens, topk, experts, device)
 
     def dispatch(self, x, ids32, ids64=None):
-        """Hot path: valid in-range int32 IDs and contiguous inputs are required."""
+        """Pack x by expert without argument checks (the block's path): ids32 must be
+        contiguous int32 in [0, experts) and x contiguous, of the workspace's shape."""
         if self.alignment == 1:
             self.extension.dispatch_out(
                 x, ids32, self.counts, self.offsets, self.slots, self.packed, self.inverse,

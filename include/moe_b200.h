@@ -146,6 +146,38 @@ int moe_grouped_gemm_swiglu(const void* packed, const void* gate_up, const int32
 int moe_grouped_gemm(const void* a, const void* weight, const int32_t* offsets, void* out,
                      int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts, void* stream);
 
+/* ------------------------------------------------------ FP8 (e4m3) experts
+ * No counterpart in the reference, whose experts are bf16 only
+ * (layer.py:97-98): an extension on tcgen05.mma.kind::f8f6f4. */
+
+/* e4m3 quantisation of bf16 rows x[rows, cols] (dtype must be BF16, cols a
+ * multiple of 16): scale[r] = amax_r / 448 and q[r, c] = e4m3(x[r, c] *
+ * (448 / amax_r)) rounded to nearest even and saturated at +-448, so
+ * x ~ q * scale; an all-zero row gets scale 1 and zeros.  Used for the packed
+ * activation rows before the e4m3 gate/up GEMM, and once for the weights
+ * (one scale per output channel = weight row). */
+int moe_quantize_rows_e4m3(const void* x, int32_t dtype, void* q, float* scale, int64_t rows,
+                           int64_t cols, void* stream);
+
+/* moe_grouped_gemm_swiglu with e4m3 operands: packed_q [rows, hidden] with
+ * packed_scale [rows], gate_up_q [experts, 2*intermediate, hidden] with
+ * gate_up_scale [experts * 2 * intermediate].  The e4m3 products are exact
+ * and accumulate in fp32; then g = bf16((acc_g * packed_scale[r]) *
+ * gate_up_scale[gate row]), u likewise, activated = bf16(silu(g) * u).
+ * hidden must be a multiple of 16. */
+int moe_grouped_gemm_swiglu_e4m3(const void* packed_q, const float* packed_scale,
+                                 const void* gate_up_q, const float* gate_up_scale,
+                                 const int32_t* offsets, void* activated, int64_t rows,
+                                 int64_t hidden, int64_t intermediate, int32_t experts,
+                                 void* stream);
+
+/* moe_grouped_gemm with e4m3 operands: out[r, c] = bf16((acc * a_scale[r]) *
+ * weight_scale[e * n_cols + c]). */
+int moe_grouped_gemm_e4m3(const void* a_q, const float* a_scale, const void* weight_q,
+                          const float* weight_scale, const int32_t* offsets, void* out,
+                          int64_t rows, int64_t n_cols, int64_t k_dim, int32_t experts,
+                          void* stream);
+
 /* Which tile the two grouped GEMMs above use for `rows` packed rows over
  * `experts` experts (no counterpart in the reference): 1 = the 256-row
  * CTA-pair tile (cta_group::2), 0 = the 128-row one-CTA tile.  Every tile

@@ -451,6 +451,54 @@ int oracle_ep_regroup(const void* from, int dtype, void* to, const int32_t* coun
     return OR_OK;
 }
 
+/* ---------------------------------------------------------------- e4m3
+ * The FP8 expert path has no counterpart in the reference (its experts are
+ * bf16 only, layer.py:97-98); this restates the engine's own definition so the
+ * GPU quantiser can be checked bit for bit.  e4m3 here is the "fn" format:
+ * 1 sign, 4 exponent bits (bias 7), 3 mantissa bits, no infinities, largest
+ * finite 448 (0x7E), NaN 0x7F, subnormals m * 2^-9.  Conversion rounds to
+ * nearest, ties to even, and saturates finite values at +-448. */
+static uint8_t f32_to_e4m3(float f) {
+    const uint8_t sign = signbit(f) ? 0x80 : 0x00;
+    if (isnan(f)) return 0x7F;
+    const double a = fabs((double)f);
+    if (a >= 448.0) return sign | 0x7E;
+    if (a < 0.015625) {                       /* below 2^-6: subnormal steps of 2^-9 */
+        const double m = nearbyint(a * 512.0);  /* 0..8; 8 is the smallest normal */
+        return sign | (uint8_t)m;               /* m = 8 encodes exponent 1, mantissa 0 */
+    }
+    int e2;
+    frexp(a, &e2);
+    int e = e2 - 1;                           /* a in [2^e, 2^(e+1)), e in -6..8 */
+    double m = nearbyint(ldexp(a, 3 - e));    /* 8..16 */
+    if (m >= 16.0) {
+        m = 8.0;
+        e += 1;
+    }
+    if (e > 8 || (e == 8 && m > 14.0)) return sign | 0x7E;
+    return sign | (uint8_t)(((e + 7) << 3) | ((int)m - 8));
+}
+
+uint8_t oracle_f32_to_e4m3(float f) { return f32_to_e4m3(f); }
+
+/* Per-row e4m3 quantisation of bf16 rows (the engine's moe_quantize_rows_e4m3):
+ * amax = max |x|, inv = 448 / amax (fp32 division), scale = amax / 448,
+ * q = e4m3(x * inv) in fp32; an all-zero row gets scale 1 and zeros. */
+int oracle_quantize_rows_e4m3(const uint16_t* x, int64_t rows, int64_t cols, uint8_t* q,
+                              float* scale) {
+    if (rows < 0 || cols < 0) return OR_EINVAL;
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+        const uint16_t* xr = x + r * cols;
+        float amax = 0.0f;
+        for (int64_t c = 0; c < cols; ++c) amax = fmaxf(amax, fabsf(bf16_to_f32(xr[c])));
+        const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+        scale[r] = amax > 0.0f ? amax / 448.0f : 1.0f;
+        for (int64_t c = 0; c < cols; ++c) q[r * cols + c] = f32_to_e4m3(bf16_to_f32(xr[c]) * inv);
+    }
+    return OR_OK;
+}
+
 int oracle_num_threads(void) {
 #ifdef _OPENMP
     return omp_get_max_threads();

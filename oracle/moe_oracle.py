@@ -51,6 +51,9 @@ def library():
         lib.oracle_f32_to_bf16.restype = ctypes.c_uint16
         lib.oracle_f32_to_f16.argtypes = [ctypes.c_float]
         lib.oracle_f32_to_f16.restype = ctypes.c_uint16
+        lib.oracle_f32_to_e4m3.argtypes = [ctypes.c_float]
+        lib.oracle_f32_to_e4m3.restype = ctypes.c_uint8
+        lib.oracle_quantize_rows_e4m3.argtypes = [p, i64, i64, p, p]
         lib.oracle_num_threads.restype = ctypes.c_int
         lib.oracle_set_num_threads.argtypes = [ctypes.c_int]
         _lib = lib
@@ -279,3 +282,19 @@ def block_forward(x, router_weight, bias, gate_up, down, topk, alignment=8):
         "output": output,
     }
 
+
+
+def f32_to_e4m3(value: float) -> int:
+    """The e4m3 byte of one fp32 value (round to nearest even, saturating)."""
+    return int(library().oracle_f32_to_e4m3(float(value)))
+
+
+def quantize_rows_e4m3(x):
+    """Per-row e4m3 quantisation of bf16 rows x[R,C] -> (q float8_e4m3fn [R,C], scale fp32 [R])."""
+    assert x.dtype == torch.bfloat16 and x.dim() == 2
+    x = x.contiguous()
+    q = torch.empty(x.shape, dtype=torch.uint8)
+    scale = torch.empty(x.shape[0], dtype=torch.float32)
+    _check(library().oracle_quantize_rows_e4m3(_ptr(x), x.shape[0], x.shape[1], _ptr(q), _ptr(scale)),
+           "oracle_quantize_rows_e4m3")
+    return q.view(torch.float8_e4m3fn), scale

@@ -23,8 +23,10 @@ Mixtral shape) and the GPU results (this engine and the reference's GPU path,
 2e-4 apart) differ by up to ~1.1e-3 relative L2 at the Mixtral shape: the bf16
 re-rounding after each GEMM turns their different fp32 accumulation into
 whole-ulp differences of the intermediates at K = 4096 and 14336.  Against the
-two CPU results the relative L2 bound is therefore 1.5e-3; against the
-reference's GPU path it is the north-star 1e-3.
+two CPU results the relative L2 bound is therefore 1.5e-3 and the max-abs
+bound two bf16 ulps of the largest output, or 1e-2 where that is larger (at
+the E=256 shape, outputs near 2 differ by 0.0156 = one ulp above 2); against
+the reference's GPU path both are the north-star 1e-2 and 1e-3.
 """
 
 from pathlib import Path
@@ -48,6 +50,13 @@ GOLDEN = {c["workload"]: c for c in torch.load(ROOT / "tests" / "golden" / "gold
                                                weights_only=True)["full_size"]}
 ROUTE_TOKENS = {"mixtral": 4096, "fine_grained": 16384, "expert_parallel": 2048}
 CPU_REL_L2 = 1.5e-3  # against the oracle and the reference's CPU path (see the module docstring)
+
+
+def cpu_max_abs(expected):
+    """1e-2, or two bf16 ulps of the largest |expected| where that is larger."""
+    top = float(expected.float().abs().max())
+    ulp = 2.0 ** (torch.floor(torch.log2(torch.tensor(top))).item() - 7) if top > 0 else 0.0
+    return max(BLOCK_MAX_ABS, 2 * ulp)
 
 
 def reference_logits(x, router, bias):
@@ -148,7 +157,7 @@ def test_full_size_block_matches_oracle_and_reference_cpu_path(full_block):
     for what, ref in (("oracle", expected), ("reference CPU path", case["output"])):
         max_abs, rel = block_error(got, ref)
         print(f"{f['name']} vs {what}: max-abs {max_abs:.4g}, rel-L2 {rel:.3g}")
-        assert max_abs <= BLOCK_MAX_ABS and rel <= CPU_REL_L2, (what, max_abs, rel)
+        assert max_abs <= cpu_max_abs(ref) and rel <= CPU_REL_L2, (what, max_abs, rel)
     assert f["block"].extension.device_status() == 0
 
 
@@ -197,6 +206,11 @@ def test_full_size_block_matches_the_reference_gpu_path(full_block):
                 ref_ids, _, _ = ref_block.route(xs)
         except RuntimeError as err:  # e.g. grouped_mm not built for this GPU
             print(f"{f['name']}: reference GPU path with {backend} GEMM unavailable: {err}")
+            continue
+        if not bool(torch.isfinite(expected).all()):
+            # seen with the reference's Triton grouped GEMM at the E=256 shape on B200
+            print(f"{f['name']}: the reference's GPU path with its {backend} GEMM returned "
+                  "non-finite outputs; not compared")
             continue
         same = (ref_ids == f["ids32"][subset]).all(dim=1)
         got = f["out"][subset]

@@ -159,3 +159,34 @@ def test_oracle_matches_reference_at_full_shapes(name):
     torch.testing.assert_close(expected["weights"], case["route_weights"], rtol=2e-5, atol=2e-5)
     max_abs, rel = block_error(expected["output"], case["output"])
     assert max_abs <= BLOCK_MAX_ABS and rel <= BLOCK_REL_L2, (max_abs, rel)
+
+
+def test_oracle_e4m3_conversion_matches_torch():
+    """The oracle's fp32 -> e4m3 conversion (round to nearest even, saturating)
+    equals torch's float8_e4m3fn conversion everywhere inside +-448, including
+    ties, subnormals and the largest finite value."""
+    grid = torch.cat([
+        torch.linspace(-448, 448, 20001),
+        torch.logspace(-12, 2.65, 4001), -torch.logspace(-12, 2.65, 4001),
+        # exact midpoints between neighbouring e4m3 values (ties go to even)
+        (torch.arange(0, 126, dtype=torch.uint8).view(torch.float8_e4m3fn).float()[:-1]
+         + torch.arange(1, 126, dtype=torch.uint8).view(torch.float8_e4m3fn).float()) / 2,
+        torch.tensor([0.0, -0.0, 448.0, -448.0, 2.0**-9, 2.0**-10, 3 * 2.0**-10]),
+    ])
+    expected = grid.to(torch.float8_e4m3fn).view(torch.uint8)
+    got = torch.tensor([oracle.f32_to_e4m3(float(v)) for v in grid], dtype=torch.uint8)
+    assert torch.equal(got, expected)
+    assert oracle.f32_to_e4m3(1000.0) == 0x7E and oracle.f32_to_e4m3(-1000.0) == 0xFE  # saturates
+
+
+def test_oracle_quantize_rows_e4m3_dequantises_close():
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(17, 256, generator=g).to(torch.bfloat16)
+    x[4] = 0
+    q, scale = oracle.quantize_rows_e4m3(x)
+    assert float(scale[4]) == 1.0 and not bool(q[4].view(torch.uint8).any())
+    deq = q.float() * scale[:, None]
+    amax = x.float().abs().max(dim=1).values
+    assert torch.allclose(q.float().abs().max(dim=1).values[amax > 0], torch.tensor(448.0))
+    # e4m3 keeps 3 mantissa bits: each element within half an e4m3 step of x
+    assert float(((deq - x.float()).abs() / (amax[:, None] + 1e-30)).max()) <= 2.0**-4
