@@ -127,6 +127,11 @@ def parse_args(argv=None):
                         help="expert-parallel exchange for N > 1 (default p2p up to 8 GPUs)")
     parser.add_argument("--ep-micro-batches", type=int, default=1,
                         help="p2p only: token slices pipelined so exchanges overlap the GEMMs")
+    parser.add_argument("--ep-overlap", type=int, choices=[0, 1], default=None,
+                        help="p2p: exchange beside the arrival-ordered gate/up GEMM (default on "
+                             "with one micro-batch)")
+    parser.add_argument("--ep-fused-return", type=int, choices=[0, 1], default=None,
+                        help="p2p: the down GEMM returns the rows itself (default: the block's)")
     parser.add_argument("--reference-gpu-worker", action="store_true", help=argparse.SUPPRESS)
     return parser.parse_args(argv)
 
@@ -289,7 +294,8 @@ def ep_tokens_per_rank(workload, world):
     return workload.tokens, "weak"
 
 
-def build_ep_block(workload, device, rank, world, backend=None, micro_batches=1):
+def build_ep_block(workload, device, rank, world, backend=None, micro_batches=1, overlap=None,
+                   fused_return=None):
     """This rank's shard of the workload: all router rows, E/world experts, its tokens."""
     from moe_dispatch.expert_parallel import ExpertParallelMoEBlock, expert_range
     from moe_dispatch.layer import MoEConfig
@@ -301,8 +307,13 @@ def build_ep_block(workload, device, rank, world, backend=None, micro_batches=1)
     gate_up, down = gpu_experts(w, device, first, local)
     if backend == "nccl" or (backend is None and world > 8):
         micro_batches = 1
+    options = {}
+    if fused_return is not None:
+        options["fused_return"] = bool(fused_return)
+    if overlap is not None and micro_batches == 1 and backend != "nccl":
+        options["overlap"] = bool(overlap)
     block = ExpertParallelMoEBlock(cfg, router, gate_up, down, device=device, routing_bias=bias,
-                                   backend=backend, micro_batches=micro_batches)
+                                   backend=backend, micro_batches=micro_batches, **options)
     tokens, _ = ep_tokens_per_rank(w, world)
     return block, gpu_tokens(w, device, tokens, rank)
 
@@ -659,6 +670,21 @@ def run_ours(args, rank, world, local):
 EP_STAGES = ("exchange", "gemm1", "gemm2", "return")
 
 
+def ep_kernels_per_step(block, workload):
+    """This engine's kernels in one expert-parallel forward (NCCL's own kernels
+    not counted): per micro-batch the route, dispatch (2), the exchange
+    kernels, the two grouped GEMMs and the combine."""
+    route = 1 if workload.experts <= 32 else 2
+    if block.backend != "p2p":
+        return route + 2 + 1 + 2 + 2 + 1  # layout, regroup x2
+    per_lane = route + 2 + 1  # route, dispatch, counts
+    per_lane += 2  # local + remote send (overlap), or send + wait for the rows
+    per_lane += 1  # gate/up GEMM
+    per_lane += 1 if block.fused_return else 2  # down GEMM (+ return copy)
+    per_lane += 1 + 1  # wait for the returns, combine
+    return per_lane * block.micro_batches
+
+
 def ep_measure(block, x, workload, args, world, device, clocks_index=None):
     """Timed expert-parallel steps (graph replay for p2p), per-stage events over
     K eager steps, the exchange bytes and the grouped rows of this rank."""
@@ -698,16 +724,17 @@ def ep_measure(block, x, workload, args, world, device, clocks_index=None):
         per_step = []
         barrier(world)
         torch.cuda.synchronize()
+        stages = EP_STAGES + (("send",) if getattr(block, "overlap", False) else ())
         for _ in range(args.steps):
             events = {n: (torch.cuda.Event(enable_timing=True),
-                          torch.cuda.Event(enable_timing=True)) for n in EP_STAGES}
+                          torch.cuda.Event(enable_timing=True)) for n in stages}
             block(x, events=events)
             per_step.append(events)
         torch.cuda.synchronize()
         barrier(world)
         del graph
     stage = {n: statistics.mean(e[n][0].elapsed_time(e[n][1]) for e in per_step)
-             for n in EP_STAGES}
+             for n in stages}
     # stage events cover the first micro-batch: count its rows only
     counts = block.last_send_counts(lane=0).view(world, -1).sum(1).tolist()
     send_rows = [int(c) for c in counts]
@@ -718,7 +745,8 @@ def ep_measure(block, x, workload, args, world, device, clocks_index=None):
         rows = block.last_grouped_rows(lane=0)
     crossing = sum(v for r, v in enumerate(send_rows) if r != block.rank) * workload.hidden * 2
     stage_max = {n: max_over_ranks(v, world, device) for n, v in stage.items()}
-    exchange_gbs = crossing / (stage["exchange"] / 1e3) / 1e9
+    # with the overlap the rows cross NVLink in the side stream's "send" stage
+    exchange_gbs = crossing / (stage.get("send", stage["exchange"]) / 1e3) / 1e9
     return_gbs = crossing / (stage["return"] / 1e3) / 1e9
     return {
         "ms_per_step": total_ms / args.steps, "stage": stage, "stage_max": stage_max,
@@ -736,7 +764,7 @@ def ep_config_leg(workload, args, rank, world, device):
     expert-parallel step, and on rank 0 the single-GPU block over all 32768
     tokens in the same run, for the strong-scaling efficiency."""
     block, x = build_ep_block(workload, device, rank, world, args.ep_backend,
-                              args.ep_micro_batches)
+                              args.ep_micro_batches, args.ep_overlap, args.ep_fused_return)
     equal, diff = ep_parity(block, x, workload, device)
     parity = all_ranks_true(equal, world, device)
     diff = max_over_ranks(diff, world, device)
@@ -784,7 +812,7 @@ def run_expert_parallel(args, rank, world, local):
     workload = WORKLOADS[args.workload]
     _, tf_peak, _, peak_kind = measured_peaks()
     block, x = build_ep_block(workload, device, rank, world, args.ep_backend,
-                              args.ep_micro_batches)
+                              args.ep_micro_batches, args.ep_overlap, args.ep_fused_return)
     tokens, scaling = ep_tokens_per_rank(workload, world)
     # -- correctness first: this rank's tokens through a single-GPU block with every expert
     equal, diff = ep_parity(block, x, workload, device)
@@ -802,6 +830,8 @@ def run_expert_parallel(args, rank, world, local):
     gemm1_kernel, tile = gemm_kernel_name(block, capacity, workload.experts // world)
     ms_per_step = m["ms_per_step"]
     graphed = m["graphed"]
+    launches = ep_kernels_per_step(block, workload)
+    block_options = {"overlap": getattr(block, "overlap", False), "fused_return": block.fused_return}
     block.close()
     del block, x
     torch.cuda.empty_cache()
@@ -828,6 +858,8 @@ def run_expert_parallel(args, rank, world, local):
             "parallelism": f"ep{world}",
             "exchange": "p2p" if graphed else "nccl",
             "micro_batches": args.ep_micro_batches,
+            "exchange_overlapped_with_gate_up": bool(block_options["overlap"]),
+            "fused_return": bool(block_options["fused_return"]),
             "timing": ("CUDA graph replay of one expert-parallel step (NVLink peer stores, no "
                        "host sync)" if graphed else
                        "eager steps (one host sync per step for the all-to-all split sizes)"),
@@ -859,7 +891,7 @@ def run_expert_parallel(args, rank, world, local):
                     "per-slot CUDA graph, result out; copies on two copy streams overlap the "
                     "neighbouring steps' compute",
         },
-        "gpu_launches": (kernels_per_step(workload.experts) + (5 if graphed else 3)) * args.steps,
+        "gpu_launches": launches * args.steps,
         "clocks": m["clocks"],
         "device_status": status,
     }

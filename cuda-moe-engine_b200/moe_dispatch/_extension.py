@@ -62,6 +62,9 @@ SIGNATURES = {
         ctypes.c_int,
         [_I32, _P, _P, _P, _P, _I32, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P],
     ),
+    "moe_ep_p2p_gate_up": (
+        ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _I64, _P]
+    ),
     "moe_ep_p2p_down_return": (
         ctypes.c_int, [_P, _P, _P, _P, _I32, _I32, _I32, _I64, _I64, _I64, _I64, _P]
     ),

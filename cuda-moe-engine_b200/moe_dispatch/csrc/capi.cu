@@ -401,20 +401,48 @@ int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* re
         return fail(MOE_ERR_INVALID, "expert-parallel P2P supports up to %d experts",
                     moe::kMaxRouteExperts);
     if (alignment < 1 || alignment > 128) return fail(MOE_ERR_INVALID, "alignment must be 1..128");
-    if (op < moe::kEpP2pCounts || op > moe::kEpP2pWaitReturn) return fail(MOE_ERR_INVALID, "bad op");
+    if (op < moe::kEpP2pCounts || op > moe::kEpP2pSendRemote) return fail(MOE_ERR_INVALID, "bad op");
     if (!regions || !state) return fail(MOE_ERR_INVALID, "null pointer");
     for (int i = 0; i < ranks; ++i)
         if (!regions[i] || !aligned(regions[i], 1024))
             return fail(MOE_ERR_INVALID, "peer regions must be non-null and 1024-byte aligned");
-    if ((op == moe::kEpP2pCounts || op == moe::kEpP2pSend) && !aux)
+    const bool sends = op == moe::kEpP2pSend || op == moe::kEpP2pSendLocal ||
+                       op == moe::kEpP2pSendRemote;
+    if ((op == moe::kEpP2pCounts || sends) && !aux)
         return fail(MOE_ERR_INVALID, "counts / dispatch offsets required");
-    if ((op == moe::kEpP2pSend || op == moe::kEpP2pReturn) && (!rows || !aligned(rows, 16)))
+    if ((sends || op == moe::kEpP2pReturn) && (!rows || !aligned(rows, 16)))
         return fail(MOE_ERR_INVALID, "rows must be non-null and 16-byte aligned");
     if (timeout_ms < 1) return fail(MOE_ERR_INVALID, "timeout_ms must be >= 1");
     return cuda_status(moe::launch_ep_p2p(op, rows, aux, regions, state, ranks, rank, experts,
                                           alignment, hidden, grouped_rows, back_rows, timeout_ms,
                                           static_cast<cudaStream_t>(stream)),
                        "moe_ep_p2p");
+}
+
+int moe_ep_p2p_gate_up(const void* gate_up, void* activated, void* const* regions, int32_t* state,
+                       int32_t ranks, int32_t rank, int32_t experts, int64_t hidden,
+                       int64_t intermediate, int64_t grouped_rows, int64_t back_rows,
+                       int64_t timeout_ms, void* stream) {
+    if (moe_ep_p2p_region_bytes(ranks, experts, hidden, grouped_rows, back_rows) < 0)
+        return fail(MOE_ERR_INVALID, "expert-parallel P2P: 1 <= ranks <= %d, experts a multiple "
+                                     "of ranks, hidden a multiple of 8", moe::kEpP2pMaxRanks);
+    if (rank < 0 || rank >= ranks) return fail(MOE_ERR_INVALID, "rank out of range");
+    if (intermediate < 8 || intermediate % 8 || grouped_rows < 1 || grouped_rows > INT_MAX)
+        return fail(MOE_ERR_INVALID, "invalid gate/up GEMM shape");
+    if (!gate_up || !activated || !regions || !state || !aligned(gate_up, 16) ||
+        !aligned(activated, 16))
+        return fail(MOE_ERR_INVALID, "null or unaligned pointer");
+    for (int i = 0; i < ranks; ++i)
+        if (!regions[i] || !aligned(regions[i], 1024))
+            return fail(MOE_ERR_INVALID, "peer regions must be non-null and 1024-byte aligned");
+    if (timeout_ms < 1) return fail(MOE_ERR_INVALID, "timeout_ms must be >= 1");
+    const char* message = nullptr;
+    cudaError_t err = moe::launch_ep_p2p_gate_up(gate_up, activated, regions, state, ranks, rank,
+                                                 experts, hidden, intermediate, grouped_rows,
+                                                 back_rows, timeout_ms,
+                                                 static_cast<cudaStream_t>(stream), &message);
+    if (message) return fail(MOE_ERR_INVALID, "%s", message);
+    return cuda_status(err, "moe_ep_p2p_gate_up");
 }
 
 int moe_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,

@@ -69,6 +69,9 @@ struct State {
     int32_t* seg_count;    // [P][E_l] rows from source s for my expert
     int32_t* ret_dst;      // [P][E_l] packed row on source s where they go back
     int32_t* recv_prefix;  // [P*E_l + 1] source-major prefix of seg_count
+    int32_t* owner_total;  // [P]  rows I send to each owner
+    int32_t* owner_done;   // [P]  rows of them stored so far (remote send)
+    int32_t* group_rows;   // [E_l][P + 1] first row of each arrival group inside my expert
 };
 
 __host__ __device__ inline State state_view(int32_t* base, int ranks, int experts) {
@@ -82,7 +85,21 @@ __host__ __device__ inline State state_view(int32_t* base, int ranks, int expert
     s.seg_count = s.seg_start + ranks * local;
     s.ret_dst = s.seg_count + ranks * local;
     s.recv_prefix = s.ret_dst + ranks * local;
+    s.owner_total = s.recv_prefix + ranks * local + 1;
+    s.owner_done = s.owner_total + ranks;
+    s.group_rows = s.owner_done + ranks;
     return s;
+}
+
+// Inside an expert's grouped span on owner o the sources' rows follow the
+// order in which they arrive: o's own rows first, then those of o-1, o-2, ...
+// (mod P) -- the shifted send schedule reaches owner o from o-1 first.  GEMM
+// rows are independent, so the order does not change any result bit.
+__host__ __device__ inline int arrival_pos(int owner, int source, int ranks) {
+    return (owner - source + ranks) % ranks;
+}
+__host__ __device__ inline int arrival_source(int owner, int pos, int ranks) {
+    return (owner - pos + ranks) % ranks;
 }
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -181,12 +198,19 @@ ep_exchange_counts_kernel(const int32_t* __restrict__ counts, Regions regions, i
     }
     __syncthreads();
     for (int e = tid; e < experts; e += blockDim.x) {
-        const int owner_first = (e / local) * local;
+        const int owner = e / local, owner_first = owner * local;
         int start = 0;
         for (int e2 = owner_first; e2 < e; ++e2) start += span[e2];
-        int before = 0;
-        for (int s = 0; s < me; ++s) before += inbox[s * experts + e];
+        int before = 0;  // rows of sources that come before me on this owner
+        for (int g = 0; g < arrival_pos(owner, me, ranks); ++g)
+            before += inbox[arrival_source(owner, g, ranks) * experts + e];
         st.send_dst[e] = start + before;
+    }
+    for (int o = tid; o < ranks; o += blockDim.x) {
+        int total = 0;
+        for (int e_l = 0; e_l < local; ++e_l) total += inbox[me * experts + o * local + e_l];
+        st.owner_total[o] = total;
+        st.owner_done[o] = 0;
     }
     if (tid == 0) {
         int run = 0;
@@ -204,10 +228,20 @@ ep_exchange_counts_kernel(const int32_t* __restrict__ counts, Regions regions, i
         st.recv_prefix[ranks * local] = run;
     }
     __syncthreads();
+    for (int e_l = tid; e_l < local; e_l += blockDim.x) {
+        const int e = me * local + e_l;
+        int run = 0;
+        for (int g = 0; g < ranks; ++g) {
+            st.group_rows[e_l * (ranks + 1) + g] = run;
+            run += inbox[arrival_source(me, g, ranks) * experts + e];
+        }
+        st.group_rows[e_l * (ranks + 1) + ranks] = run;
+    }
     for (int i = tid; i < ranks * local; i += blockDim.x) {
         const int s = i / local, e_l = i % local, e = me * local + e_l;
         int before = 0;
-        for (int s2 = 0; s2 < s; ++s2) before += inbox[s2 * experts + e];
+        for (int g = 0; g < arrival_pos(me, s, ranks); ++g)
+            before += inbox[arrival_source(me, g, ranks) * experts + e];
         st.seg_start[i] = st.offsets[e_l] + before;
         st.seg_count[i] = inbox[s * experts + e];
         int packed = 0;  // source s packs compactly, expert-major
@@ -218,7 +252,21 @@ ep_exchange_counts_kernel(const int32_t* __restrict__ counts, Regions regions, i
     if (tid == 0) *st.epoch = static_cast<int32_t>(epoch);
 }
 
+// Which rows a send launch moves.
+enum SendMode { kSendAll = 0, kSendLocal = 1, kSendRemote = 2 };
+
 // Rows of my compact packed buffer -> their owners' grouped buffers (a warp per row).
+//   kSendAll     every row; the last CTA raises the rows flag of source `me`
+//                on every rank.
+//   kSendLocal   only the rows of my own experts (an HBM copy); no flag -- the
+//                launches after it on the stream see them.
+//   kSendRemote  only the rows of other ranks' experts.  Each warp counts its
+//                stored row for the row's owner; the warp that completes an
+//                owner's rows raises the rows flag of source `me` on that owner,
+//                so an owner can start on my rows while I still send to others.
+//                CTA 0 raises it at once on owners I send nothing, and on
+//                myself (my own rows are kSendLocal's, ordered by the stream).
+template <int kMode>
 __global__ void __launch_bounds__(kCopyThreads)
 ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict__ dispatch_offsets,
                     Regions regions, int32_t* state_base, int ranks, int me, int experts,
@@ -226,16 +274,38 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
     const Layout l = region_layout(ranks, experts, hidden, grouped_rows, back_rows);
     State st = state_view(state_base, ranks, experts);
     const int local = experts / ranks;
-    const int64_t rows = dispatch_offsets[experts];
     const int lane = threadIdx.x & 31;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (kCopyThreads / 32);
-    // Start at the rows for rank me+1 and wrap around: at any moment the ranks
-    // write to different owners (a shifted all-to-all), instead of every rank
-    // writing to owner 0 first.
-    const int64_t rotate = dispatch_offsets[((me + 1) % ranks) * local];
+    const uint32_t epoch = static_cast<uint32_t>(*st.epoch);
+    const int64_t total = dispatch_offsets[experts];
+    // Rows to walk: `rows` of them from packed row `first + rotate` on, wrapping.
+    int64_t first = 0, rows = total, rotate = 0;
+    if (kMode == kSendLocal) {
+        first = dispatch_offsets[me * local];
+        rows = dispatch_offsets[(me + 1) * local] - first;
+    } else {
+        // Start at the rows for rank me+1 and wrap around: at any moment the
+        // ranks write to different owners (a shifted all-to-all), instead of
+        // every rank writing to owner 0 first.
+        rotate = dispatch_offsets[((me + 1) % ranks) * local];
+        if (kMode == kSendRemote) {
+            // my own rows are the range [a, b): walk b .. a (mod total)
+            const int64_t a = dispatch_offsets[me * local], b = dispatch_offsets[(me + 1) * local];
+            rows -= b - a;
+            rotate = b;
+        }
+    }
+    if (kMode == kSendRemote && blockIdx.x == 0 && static_cast<int>(threadIdx.x) < ranks) {
+        const int o = threadIdx.x;
+        if (o == me || st.owner_total[o] == 0) {
+            uint32_t* flags = reinterpret_cast<uint32_t*>(regions.base[o] + l.flags);
+            store_release_sys(flags + kMaxRanks + me, epoch);
+        }
+    }
     for (int64_t v = (static_cast<int64_t>(blockIdx.x) * kCopyThreads + threadIdx.x) >> 5; v < rows;
          v += warps) {
-        const int64_t r = v + rotate < rows ? v + rotate : v + rotate - rows;
+        int64_t r = first + v + rotate;
+        if (r >= total) r -= total;
         int lo = 0, hi = experts - 1;  // expert of packed row r
         while (lo < hi) {
             const int mid = (lo + hi + 1) >> 1;
@@ -250,7 +320,17 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
         }
         uint4* target = reinterpret_cast<uint4*>(regions.base[owner] + l.grouped) + dst * row_vecs;
         warp_copy_row(target, packed + r * row_vecs, row_vecs, lane);
+        if (kMode == kSendRemote) {
+            __threadfence_system();  // this lane's part of the row is visible on the owner
+            __syncwarp();
+            if (lane == 0 && atomicAdd(&st.owner_done[owner], 1) + 1 == st.owner_total[owner]) {
+                st.owner_done[owner] = 0;  // every row counted: ready for the next step
+                uint32_t* flags = reinterpret_cast<uint32_t*>(regions.base[owner] + l.flags);
+                store_release_sys(flags + kMaxRanks + me, epoch);
+            }
+        }
     }
+    if (kMode != kSendAll) return;
     // the last CTA to finish raises the rows flag of source `me` on every rank
     __threadfence_system();
     __syncthreads();
@@ -261,7 +341,7 @@ ep_send_rows_kernel(const uint4* __restrict__ packed, const int32_t* __restrict_
     __threadfence_system();
     if (threadIdx.x < ranks) {
         uint32_t* flags = reinterpret_cast<uint32_t*>(regions.base[threadIdx.x] + l.flags);
-        store_release_sys(flags + kMaxRanks + me, static_cast<uint32_t>(*st.epoch));
+        store_release_sys(flags + kMaxRanks + me, epoch);
     }
     if (threadIdx.x == 0) st.counters[0] = 0;
 }
@@ -335,6 +415,17 @@ unsigned copy_grid() {
     return grid;
 }
 
+// Grid of the remote send, which runs beside the gate/up GEMM: one CTA per
+// SM of a B200 (each fits beside a GEMM CTA); MOE_B200_EP_SEND_CTAS=n overrides.
+unsigned remote_send_grid() {
+    static const unsigned grid = [] {
+        const char* env = getenv("MOE_B200_EP_SEND_CTAS");
+        const int n = env ? atoi(env) : 0;
+        return static_cast<unsigned>(n > 0 && n <= 148 * 8 ? n : 148);
+    }();
+    return grid;
+}
+
 Regions to_regions(void* const* regions, int ranks) {
     Regions r = {};
     for (int i = 0; i < ranks; ++i) r.base[i] = static_cast<char*>(regions[i]);
@@ -356,7 +447,8 @@ int64_t ep_p2p_region_offset(int ranks, int experts, int64_t hidden, int64_t gro
 
 int64_t ep_p2p_state_words(int ranks, int experts) {
     const int local = experts / ranks;
-    return 4 + experts + (local + 1) + 3 * ranks * local + ranks * local + 1;
+    return 4 + experts + (local + 1) + 3 * ranks * local + ranks * local + 1 + 2 * ranks +
+           local * (ranks + 1);
 }
 
 cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* const* regions,
@@ -375,9 +467,19 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
             break;
         }
         case kEpP2pSend:
-            ep_send_rows_kernel<<<copy_grid(), kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), aux, r,
-                                                             state, ranks, me, experts, row_vecs,
-                                                             hidden, grouped_rows, back_rows);
+            ep_send_rows_kernel<kSendAll><<<copy_grid(), kCopyThreads, 0, stream>>>(
+                static_cast<const uint4*>(rows), aux, r, state, ranks, me, experts, row_vecs, hidden,
+                grouped_rows, back_rows);
+            break;
+        case kEpP2pSendLocal:
+            ep_send_rows_kernel<kSendLocal><<<copy_grid(), kCopyThreads, 0, stream>>>(
+                static_cast<const uint4*>(rows), aux, r, state, ranks, me, experts, row_vecs, hidden,
+                grouped_rows, back_rows);
+            break;
+        case kEpP2pSendRemote:
+            ep_send_rows_kernel<kSendRemote><<<remote_send_grid(), kCopyThreads, 0, stream>>>(
+                static_cast<const uint4*>(rows), aux, r, state, ranks, me, experts, row_vecs, hidden,
+                grouped_rows, back_rows);
             break;
         case kEpP2pReturn:
             ep_return_rows_kernel<<<copy_grid(), kCopyThreads, 0, stream>>>(static_cast<const uint4*>(rows), r,
@@ -394,6 +496,26 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
             return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_ep_p2p_gate_up(const void* gate_up, void* activated, void* const* regions,
+                                  int32_t* state, int ranks, int me, int experts, int64_t hidden,
+                                  int64_t intermediate, int64_t grouped_rows, int64_t back_rows,
+                                  int64_t timeout_ms, cudaStream_t stream, const char** error) {
+    const Layout l = region_layout(ranks, experts, hidden, grouped_rows, back_rows);
+    const State st = state_view(state, ranks, experts);
+    GemmArrival arrival;
+    arrival.groups = ranks;
+    arrival.group_rows = st.group_rows;
+    arrival.flags = reinterpret_cast<const uint32_t*>(static_cast<char*>(regions[me]) + l.flags) + kMaxRanks;
+    arrival.epoch = st.epoch;
+    arrival.ranks = ranks;
+    arrival.me = me;
+    arrival.limit_ns = static_cast<uint64_t>(timeout_ms) * 1000000ull;
+    const void* grouped = static_cast<char*>(regions[me]) + l.grouped;
+    return launch_grouped_gemm(grouped, gate_up, st.offsets, activated, grouped_rows, intermediate,
+                               hidden, experts / ranks, true, stream, error, nullptr, nullptr,
+                               ranks > 1 ? &arrival : nullptr);
 }
 
 cudaError_t launch_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,

@@ -54,6 +54,7 @@ constexpr int kTileBBytes = kBN * kBK * 2;
 constexpr int kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kBoxRows = 128;
 constexpr int kBoxBytes = kBoxRows * kBK * 2;
+constexpr int kPairBM = 2 * kBM;  // rows of the CTA-pair tile
 constexpr int kTmemCols = 2 * kBN;
 // Warps 0 and 1 load and issue; warps 2..9 are the epilogue, two per TMEM lane
 // quarter (and so two per SM sub-partition), each taking half of a tile's
@@ -69,10 +70,17 @@ constexpr uint64_t kDrainLimitNs = 200000000ull;   // bounded drain after an err
 
 constexpr int kTileRing = 4;                      // tiles claimed ahead of the consumers
 constexpr int kBarrierBytes = (2 * kStages + 5 + 2 * kTileRing) * 8;
+// shared tables: m-tile prefix [pairs+1], offsets [E+1], first row of each pair [pairs]
+constexpr int kTableBytes = (3 * kMaxExperts + 2) * 4;
 constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarrierBytes + 16 + kTileRing * 4 +
-                           2 * (kMaxExperts + 1) * 4;
+                           kTableBytes;
 
-enum GemmStatus : int32_t { kStatusOk = 0, kStatusWaitTimeout = 1, kStatusSlotShared = 5 };
+enum GemmStatus : int32_t {
+    kStatusOk = 0,
+    kStatusWaitTimeout = 1,
+    kStatusSlotShared = 5,
+    kStatusArrivalTimeout = 6,  // rows from a peer rank did not arrive in time
+};
 
 __device__ int32_t g_gemm_status;
 
@@ -107,7 +115,61 @@ struct GemmParams {
     uint32_t* sched;     // this launch's {claim counter, CTAs finished, CTAs entered}
     const float* a_scale;  // e4m3 operands: dequantisation scale per A row
     const float* b_scale;  // e4m3 operands: dequantisation scale per weight row
+    // Arrival groups (expert parallelism): an expert's rows come from `groups`
+    // ranks one after another; group_rows[e * (groups + 1) + g] is the first row
+    // (relative to the expert's span) of group g, group_rows[.. + groups] the
+    // expert's real rows.  A tile belongs to the group of its last real row
+    // and is loaded once arrival[source of that group and every group before]
+    // reaches *epoch (group g comes from rank (me - g) mod ranks; group 0 is
+    // this rank's own rows, already in place).  groups == 1: no waits.
+    int groups;
+    const int32_t* group_rows;
+    const uint32_t* arrival;
+    const int32_t* epoch;
+    int ranks, me;
+    uint64_t arrival_limit_ns;
 };
+
+// m-tile table of a launch, built by one warp: for every (group, expert) pair
+// j = g * experts + e, the first row of its first tile and the exclusive prefix
+// of the pairs' m-tile counts; with one group j = e.  Tiles of BM rows.
+template <int BM>
+__device__ void build_tile_table(const GemmParams& p, int lane, int* mt_prefix, int* offs,
+                                 int* tbase) {
+    for (int e = lane; e <= p.experts; e += 32) offs[e] = p.offsets[e];
+    __syncwarp();
+    const int pairs = p.experts * p.groups;
+    int carry = 0;
+    for (int j0 = 0; j0 < pairs; j0 += 32) {
+        const int j = j0 + lane;
+        int mt = 0;
+        if (j < pairs) {
+            const int e = j % p.experts, g = j / p.experts;
+            const int lo = offs[e], hi = offs[e + 1];
+            const int rows = hi - lo;
+            const int tiles = rows > 0 ? (rows + BM - 1) / BM : 0;
+            int first = 0;  // first m-tile of the pair
+            mt = tiles;
+            if (p.groups > 1) {
+                // tiles whose last real row lies in groups 0..g-1, and 0..g
+                const int* b = p.group_rows + static_cast<int64_t>(e) * (p.groups + 1);
+                const int real = b[p.groups];
+                first = g == 0 ? 0 : (b[g] >= real ? tiles : b[g] / BM);
+                mt = (b[g + 1] >= real ? tiles : b[g + 1] / BM) - first;
+            }
+            tbase[j] = lo + first * BM;
+        }
+        int inclusive = mt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+            if (lane >= off) inclusive += y;
+        }
+        if (j < pairs) mt_prefix[j] = carry + inclusive - mt;
+        carry += __shfl_sync(0xffffffffu, inclusive, 31);
+    }
+    if (lane == 0) mt_prefix[pairs] = carry;
+}
 
 // ---------------------------------------------------------------- PTX helpers
 
@@ -305,22 +367,69 @@ __device__ __forceinline__ void finish_schedule(uint32_t* sched) {
     }
 }
 
-// Tile t -> (expert, m-tile, n-tile).  Tiles are ordered by expert; inside an
-// expert by n-tile, then m-tile.
-__device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int experts, int n_tiles,
-                                            int& e, int& m, int& n) {
+// Tile t -> (pair j, m-tile inside the pair, n-tile).  Tiles are ordered by
+// pair (group-major, then expert); inside a pair by n-tile, then m-tile.
+__device__ __forceinline__ void decode_tile(int t, const int* mt_prefix, int pairs, int n_tiles,
+                                            int& j, int& m, int& n) {
     const int q = t / n_tiles;
-    int lo = 0, hi = experts - 1;
+    int lo = 0, hi = pairs - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
         if (mt_prefix[mid] <= q) lo = mid;
         else hi = mid - 1;
     }
-    e = lo;
-    const int mt = mt_prefix[e + 1] - mt_prefix[e];
-    const int local = t - mt_prefix[e] * n_tiles;
+    j = lo;
+    const int mt = mt_prefix[j + 1] - mt_prefix[j];
+    const int local = t - mt_prefix[j] * n_tiles;
     n = local / mt;
     m = local - n * mt;
+}
+
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* addr) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+    return v;
+}
+
+// Producer side of the arrival groups: before the loads of a tile of group g,
+// wait (bounded) until the rows of groups arrived+1..g are in place.  The
+// rows were written by peers; the proxy fence orders the acquire before the
+// TMA (async proxy) reads of them.  Returns false when the CTA is aborting.
+__device__ __noinline__ bool wait_arrival(const GemmParams& p, int g, int& arrived,
+                                          volatile int* abort_flag) {
+    const uint32_t epoch = static_cast<uint32_t>(*p.epoch);
+    for (int gg = arrived + 1; gg <= g; ++gg) {
+        const int src = (p.me - gg + p.ranks) % p.ranks;
+        const uint64_t start = global_timer();
+        for (uint32_t i = 0; load_acquire_sys(p.arrival + src) < epoch; ++i) {
+            if (*abort_flag) return false;
+            if ((i & 63) == 63 && global_timer() - start > p.arrival_limit_ns) {
+                record_status(kStatusArrivalTimeout);
+                *abort_flag = 1;
+                return false;
+            }
+            __nanosleep(128);
+        }
+        arrived = gg;
+    }
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+    return true;
+}
+
+// Called by one thread of every CTA of a scatter launch after its stores: the
+// last CTA to finish raises this rank's return flag on every rank.
+__device__ __forceinline__ void raise_return_flags(const GemmScatter& scatter) {
+    __threadfence_system();
+    if (atomicAdd(scatter.ticket, 1) == static_cast<int>(gridDim.x) - 1) {
+        __threadfence_system();
+        const uint32_t epoch = static_cast<uint32_t>(*scatter.epoch);
+        for (int r = 0; r < scatter.ranks; ++r) {
+            uint32_t* flag = reinterpret_cast<uint32_t*>(scatter.base[r] + scatter.flags_offset) +
+                             2 * kGemmScatterMaxRanks + scatter.me;
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
+        }
+        *scatter.ticket = 0;
+    }
 }
 
 template <bool kSwiglu, bool kScatter = false, bool kFp8 = false>
@@ -346,6 +455,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
     int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
     int* offs = mt_prefix + kMaxExperts + 1;  // shared copy of p.offsets: no global load per tile
+    int* tbase = offs + kMaxExperts + 1;      // first row of each pair's first tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;
@@ -353,29 +463,9 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
 
-    // m-tiles per expert -> exclusive prefix (warp 0).
+    // m-tile table (warp 0).
     if (warp == 0) {
-        int carry = 0;
-        for (int e0 = 0; e0 < p.experts; e0 += 32) {
-            const int e = e0 + lane;
-            int mt = 0;
-            if (e < p.experts) {
-                const int lo = p.offsets[e], hi = p.offsets[e + 1];
-                offs[e] = lo;
-                if (e == p.experts - 1) offs[p.experts] = hi;
-                const int rows = hi - lo;
-                mt = rows > 0 ? (rows + kBM - 1) / kBM : 0;
-            }
-            int inclusive = mt;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
-                if (lane >= off) inclusive += y;
-            }
-            if (e < p.experts) mt_prefix[e] = carry + inclusive - mt;
-            carry += __shfl_sync(0xffffffffu, inclusive, 31);
-        }
-        if (lane == 0) mt_prefix[p.experts] = carry;
+        build_tile_table<kBM>(p, lane, mt_prefix, offs, tbase);
     } else if (warp == 1) {
         if (lane == 0) {
             for (int s = 0; s < kStages; ++s) {
@@ -404,7 +494,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int total_tiles = mt_prefix[p.experts] * p.n_tiles;
+    const int pairs = p.experts * p.groups;
+    const int total_tiles = mt_prefix[pairs] * p.n_tiles;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -415,6 +506,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
             uint32_t last_parity = 0;      // parity of each stage's latest arm
             int ring = 0;
             uint32_t ring_phase = 0;
+            int arrived = 0;  // arrival groups known to be in place
             // One claim is kept in reserve, so the atomic's round trip overlaps
             // the previous tile's loads instead of stalling the pipeline.
             int next = claim_tile(p.sched, total_tiles);
@@ -430,9 +522,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 }
                 if (t < 0) break;
                 next = claim_tile(p.sched, total_tiles);
-                int e, m, n;
-                decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
-                const int row0 = offs[e] + m * kBM;
+                int j, m, n;
+                decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+                const int e = j % p.experts;
+                if (j / p.experts > arrived && !wait_arrival(p, j / p.experts, arrived, abort_flag)) break;
+                const int row0 = tbase[j] + m * kBM;
                 const int brow = e * p.b_rows + n * kOutTile;
                 const int brow2 = kSwiglu ? brow + p.up_offset : brow + kBoxRows;
                 bool ok = true;
@@ -534,13 +628,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 ring_phase ^= 1u;
             }
             if (t < 0) break;
-            int e, m, n;
-            decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+            int j, m, n;
+            decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+            const int e = j % p.experts;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(offs[e]) + m * kBM + quarter * 32 + lane;
+            const int64_t row = static_cast<int64_t>(tbase[j]) + m * kBM + quarter * 32 + lane;
             bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
@@ -640,20 +735,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
     if (threadIdx.x == 0) finish_schedule(p.sched);
     if constexpr (kScatter) {
-        // the last CTA to finish raises this rank's return flag on every rank
-        if (threadIdx.x == 0) {
-            __threadfence_system();
-            if (atomicAdd(scatter.ticket, 1) == static_cast<int>(gridDim.x) - 1) {
-                __threadfence_system();
-                const uint32_t epoch = static_cast<uint32_t>(*scatter.epoch);
-                for (int r = 0; r < scatter.ranks; ++r) {
-                    uint32_t* flag = reinterpret_cast<uint32_t*>(scatter.base[r] + scatter.flags_offset) +
-                                     2 * kGemmScatterMaxRanks + scatter.me;
-                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(flag), "r"(epoch) : "memory");
-                }
-                *scatter.ticket = 0;
-            }
-        }
+        if (threadIdx.x == 0) raise_return_flags(scatter);
     }
 }
 
@@ -675,8 +757,14 @@ constexpr int kPairTileBBytes = kBoxRows * kBK * 2; // this CTA's 128 rows of B
 constexpr int kPairStageBytes = kPairTileABytes + kPairTileBBytes;
 constexpr int kPairBarrierBytes = (2 * kPairStages + 5 + 2 * kTileRing) * 8;
 constexpr int kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + kPairBarrierBytes + 16 +
-                               kTileRing * 4 + 2 * (kMaxExperts + 1) * 4;
-constexpr int kPairBM = 2 * kBM;
+                               kTileRing * 4 + kTableBytes;
+// The scatter (fused return) epilogue stages each warp's 32 x 32 output chunk
+// in 2 KiB of shared memory after the tables, to store it as row segments.
+constexpr int kScatterStageOffset =
+    (kPairStages * kPairStageBytes + kPairBarrierBytes + 16 + kTileRing * 4 + kTableBytes + 15) / 16 * 16;
+constexpr int kScatterStageBytes = (kEpilogueThreads / 32) * 2048;
+constexpr int kPairScatterSmemBytes = 1024 + kScatterStageOffset + kScatterStageBytes;
+static_assert(kPairScatterSmemBytes <= 227 * 1024, "scatter epilogue staging fits in shared memory");
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
     uint32_t r;
@@ -748,10 +836,12 @@ __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
         : "memory");
 }
 
-template <bool kSwiglu, bool kFp8 = false>
+template <bool kSwiglu, bool kFp8 = false, bool kScatter = false>
 __global__ void __launch_bounds__(kThreads, 1)
 grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p) {
+                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p,
+                         const GemmScatter scatter) {
+    static_assert(!(kScatter && (kSwiglu || kFp8)), "the scatter epilogue is for the bf16 down GEMM");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -768,6 +858,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
     int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
     int* offs = mt_prefix + kMaxExperts + 1;  // shared copy of p.offsets: no global load per tile
+    int* tbase = offs + kMaxExperts + 1;      // first row of each pair's first tile
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
@@ -777,29 +868,9 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
 
-    // m-tiles (256 rows) per expert -> exclusive prefix (warp 0, both CTAs).
+    // m-tile table of 256-row tiles (warp 0, both CTAs).
     if (warp == 0) {
-        int carry = 0;
-        for (int e0 = 0; e0 < p.experts; e0 += 32) {
-            const int e = e0 + lane;
-            int mt = 0;
-            if (e < p.experts) {
-                const int lo = p.offsets[e], hi = p.offsets[e + 1];
-                offs[e] = lo;
-                if (e == p.experts - 1) offs[p.experts] = hi;
-                const int rows = hi - lo;
-                mt = rows > 0 ? (rows + kPairBM - 1) / kPairBM : 0;
-            }
-            int inclusive = mt;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
-                if (lane >= off) inclusive += y;
-            }
-            if (e < p.experts) mt_prefix[e] = carry + inclusive - mt;
-            carry += __shfl_sync(0xffffffffu, inclusive, 31);
-        }
-        if (lane == 0) mt_prefix[p.experts] = carry;
+        build_tile_table<kPairBM>(p, lane, mt_prefix, offs, tbase);
     } else if (warp == 1) {
         if (lane == 0) {
             for (int s = 0; s < kPairStages; ++s) {
@@ -830,7 +901,8 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int total_tiles = mt_prefix[p.experts] * p.n_tiles;
+    const int pairs = p.experts * p.groups;
+    const int total_tiles = mt_prefix[pairs] * p.n_tiles;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -840,6 +912,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             uint32_t armed = 0, last_parity = 0;
             int ring = 0;
             uint32_t ring_phase = 0;
+            int arrived = 0;  // arrival groups known to be in place (each CTA waits for its own rows)
             // the leader keeps one claim in reserve (see the one-CTA kernel)
             int next = leader ? claim_tile(p.sched, total_tiles) : -1;
             for (;;) {
@@ -862,9 +935,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 }
                 if (t < 0) break;
                 if (leader) next = claim_tile(p.sched, total_tiles);
-                int e, m, n;
-                decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
-                const int row0 = offs[e] + m * kPairBM + static_cast<int>(rank) * kBM;
+                int j, m, n;
+                decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+                const int e = j % p.experts;
+                if (j / p.experts > arrived && !wait_arrival(p, j / p.experts, arrived, abort_flag)) break;
+                const int row0 = tbase[j] + m * kPairBM + static_cast<int>(rank) * kBM;
                 const int brow0 = e * p.b_rows + n * kOutTile;
                 const int brow = kSwiglu ? brow0 + (leader ? 0 : p.up_offset)
                                          : brow0 + static_cast<int>(rank) * kBoxRows;
@@ -966,21 +1041,38 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                 ring_phase ^= 1u;
             }
             if (t < 0) break;
-            int e, m, n;
-            decode_tile(t, mt_prefix, p.experts, p.n_tiles, e, m, n);
+            int j, m, n;
+            decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+            const int e = j % p.experts;
             const int acc = local & 1;
             const uint32_t acc_phase = (local >> 1) & 1;
             if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
             tc_fence_after();
-            const int64_t row = static_cast<int64_t>(offs[e]) + m * kPairBM +
+            const int64_t row = static_cast<int64_t>(tbase[j]) + m * kPairBM +
                                 static_cast<int>(rank) * kBM + quarter * 32 + lane;
-            const bool valid = row < offs[e + 1];
+            bool valid = row < offs[e + 1];
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
             __nv_bfloat16* dst_row = p.out + row * p.ldo;
             // e4m3: out = bf16((acc * row scale) * column scale); the row scale is
             // read once per tile, the column scales once per 32-column chunk
             float rscale = 1.0f, gscale = 1.0f, uscale = 1.0f;
             if constexpr (kFp8) rscale = valid ? __ldg(p.a_scale + row) : 0.0f;
+            if constexpr (kScatter) {
+                // the source rank and packed row this grouped row returns to
+                valid = false;
+                for (int src = 0; src < scatter.ranks; ++src) {
+                    const int seg = src * scatter.local_experts + e;
+                    const int64_t start = scatter.seg_start[seg];
+                    if (row >= start && row < start + scatter.seg_count[seg]) {
+                        const int64_t back = scatter.ret_dst[seg] + (row - start);
+                        if (back < scatter.back_rows) {
+                            valid = true;
+                            dst_row = reinterpret_cast<__nv_bfloat16*>(
+                                          scatter.base[src] + scatter.back_offset) + back * p.ldo;
+                        }
+                    }
+                }
+            }
 #pragma unroll 1
             for (int c = group * (kOutTile / kEpilogueGroups); c < (group + 1) * (kOutTile / kEpilogueGroups);
                  c += 32) {
@@ -1032,7 +1124,32 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                         outw[j] = pack_bf16x2(lo, hi);
                     }
                 }
-                if (valid) {
+                if constexpr (kScatter) {
+                    // Rows go to peer ranks: instead of 32 scattered 16-byte
+                    // pieces per store instruction (one row per lane), stage
+                    // the 32 x 32 chunk in shared memory and store 64-byte row
+                    // segments (lanes 4r..4r+3 write row r, 8 rows per
+                    // instruction).  16-byte chunk q of row r sits at slot
+                    // q ^ ((r >> 1) & 3): conflict-free writes and reads.
+                    uint4* stage = reinterpret_cast<uint4*>(smem + kScatterStageOffset) + (warp - 2) * 128;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        stage[lane * 4 + (q ^ ((lane >> 1) & 3))] =
+                            make_uint4(outw[4 * q], outw[4 * q + 1], outw[4 * q + 2], outw[4 * q + 3]);
+                    __syncwarp();
+                    const int col0 = n * kOutTile + c;
+                    const unsigned long long my_dst = reinterpret_cast<unsigned long long>(dst_row);
+#pragma unroll
+                    for (int step = 0; step < 4; ++step) {
+                        const int r = step * 8 + (lane >> 2), q = lane & 3;
+                        const uint4 v = stage[r * 4 + (q ^ ((r >> 1) & 3))];
+                        const unsigned long long d = __shfl_sync(0xffffffffu, my_dst, r);
+                        const int ok = __shfl_sync(0xffffffffu, valid ? 1 : 0, r);
+                        if (ok && col0 + q * 8 + 8 <= p.n_out)
+                            *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(d) + col0 + q * 8) = v;
+                    }
+                    __syncwarp();
+                } else if (valid) {
                     const int col0 = n * kOutTile + c;
 #pragma unroll
                     for (int q = 0; q < 4; ++q) {
@@ -1045,6 +1162,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
             tc_fence_before();
             mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
         }
+        if constexpr (kScatter) __threadfence_system();  // results visible on their ranks
     }
 
     tc_fence_before();
@@ -1055,6 +1173,9 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      "r"(kTmemCols));
     }
     if (threadIdx.x == 0) finish_schedule(p.sched);
+    if constexpr (kScatter) {
+        if (threadIdx.x == 0) raise_return_flags(scatter);
+    }
 }
 
 // ------------------------------------------------------------------ host side
@@ -1143,7 +1264,7 @@ Tile pick_tile(int64_t rows, int experts) {
 template <typename Kernel>
 cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& resident_clusters,
                         int sms, int64_t max_tiles, const CUtensorMap& map_a, const CUtensorMap& map_b,
-                        const GemmParams& p, cudaStream_t stream) {
+                        const GemmParams& p, cudaStream_t stream, const GemmScatter& scatter = {}) {
     cudaLaunchConfig_t config = {};
     cudaLaunchAttribute attribute[1];
     attribute[0].id = cudaLaunchAttributeClusterDimension;
@@ -1168,7 +1289,7 @@ cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& re
     }
     const int64_t clusters = max_tiles < resident_clusters ? max_tiles : resident_clusters;
     config.gridDim = dim3(static_cast<unsigned>(2 * clusters));
-    return cudaLaunchKernelEx(&config, kernel, map_a, map_b, p);
+    return cudaLaunchKernelEx(&config, kernel, map_a, map_b, p, scatter);
 }
 
 }  // namespace
@@ -1176,12 +1297,14 @@ cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& re
 cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
                                 int64_t rows, int64_t n_out, int64_t k_dim, int experts,
                                 bool swiglu, cudaStream_t stream, const char** error,
-                                const float* a_scale, const float* b_scale) {
+                                const float* a_scale, const float* b_scale,
+                                const GemmArrival* arrival) {
     const bool fp8 = a_scale != nullptr;
     *error = nullptr;
     if (rows == 0 || experts == 0) return cudaSuccess;
-    if (experts > kMaxExperts) {
-        *error = "grouped GEMM supports at most 1024 experts";
+    const int groups = arrival ? arrival->groups : 1;
+    if (groups < 1 || static_cast<int64_t>(experts) * groups > kMaxExperts) {
+        *error = "grouped GEMM supports at most 1024 experts (times arrival groups)";
         return cudaErrorInvalidValue;
     }
     int device = 0;
@@ -1208,6 +1331,13 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     p.n_tiles = static_cast<int>((n_out + out_tile - 1) / out_tile);
     p.b_rows = static_cast<int>(b_rows);
     p.up_offset = swiglu ? static_cast<int>(n_out) : 0;
+    p.groups = groups;
+    p.group_rows = arrival ? arrival->group_rows : nullptr;
+    p.arrival = arrival ? arrival->flags : nullptr;
+    p.epoch = arrival ? arrival->epoch : nullptr;
+    p.ranks = arrival ? arrival->ranks : 1;
+    p.me = arrival ? arrival->me : 0;
+    p.arrival_limit_ns = arrival ? arrival->limit_ns : 0;
     MOE_CUDA_TRY(schedule_slot(info, stream, &p.sched));
 
     const Tile tile = pick_tile(rows, experts);
@@ -1246,6 +1376,7 @@ cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int3
     DeviceInfo& info = device_info(device);
     if (info.sms == 0) MOE_CUDA_TRY(cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device));
     static bool configured[64] = {};
+    static bool pair_configured[64] = {};
     auto kernel = grouped_gemm_kernel<false, true>;
     if (!configured[device & 63]) {
         MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
@@ -1269,8 +1400,22 @@ cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int3
     p.b_rows = static_cast<int>(n_out);
     p.up_offset = 0;
     p.a_scale = p.b_scale = nullptr;
+    p.groups = 1;
+    p.group_rows = nullptr;
+    p.arrival = nullptr;
+    p.epoch = nullptr;
+    p.ranks = 1;
+    p.me = 0;
+    p.arrival_limit_ns = 0;
     MOE_CUDA_TRY(schedule_slot(info, stream, &p.sched));
-    // every CTA takes part in the completion ticket, so the grid never depends on the rows
+    // Every CTA takes part in the completion ticket, so the grid never depends
+    // on the rows (rows = the grouped capacity, an upper bound).
+    if (pick_tile(rows, experts) == Tile::kPair) {
+        static int resident[64] = {};  // every resident cluster, whatever the rows
+        return launch_pair(grouped_gemm_pair_kernel<false, false, true>, kPairScatterSmemBytes,
+                           pair_configured[device & 63], resident[device & 63], info.sms, INT64_MAX,
+                           map_a, map_b, p, stream, scatter);
+    }
     kernel<<<info.sms, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, scatter);
     return cudaGetLastError();
 }

@@ -35,6 +35,22 @@ cudaError_t launch_swiglu(const void* projection, int dtype, const int32_t* vali
                           void* output, int64_t rows, int64_t width, int vector_bytes,
                           cudaStream_t stream);
 
+// Rows that arrive from peer ranks while a grouped GEMM runs (P2P expert
+// parallelism): each expert's rows are `groups` consecutive arrival groups,
+// group g from rank (me - g) mod ranks (group 0 = this rank's own rows, in
+// place before the launch).  group_rows[e * (groups + 1) + g] is the first row
+// of group g relative to the expert's span, [.. + groups] its real rows.  The
+// GEMM takes tiles group by group and loads a tile of group g once flags[s]
+// >= *epoch for the sources s of groups 1..g (bounded by limit_ns; status 6).
+struct GemmArrival {
+    int groups;
+    const int32_t* group_rows;
+    const uint32_t* flags;
+    const int32_t* epoch;
+    int ranks, me;
+    uint64_t limit_ns;
+};
+
 // Grouped GEMMs on tcgen05 (gemm_sm100.cu).  `error` receives a message when
 // the returned status is not cudaSuccess because of a host-side check.
 // With a_scale (and b_scale) non-null, a and b are e4m3 bytes and every
@@ -42,7 +58,8 @@ cudaError_t launch_swiglu(const void* projection, int dtype, const int32_t* vali
 cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* offsets, void* out,
                                 int64_t rows, int64_t n_out, int64_t k_dim, int experts,
                                 bool swiglu, cudaStream_t stream, const char** error,
-                                const float* a_scale = nullptr, const float* b_scale = nullptr);
+                                const float* a_scale = nullptr, const float* b_scale = nullptr,
+                                const GemmArrival* arrival = nullptr);
 // e4m3 quantisation of bf16 rows: scale[r] = amax_r / 448, q[r,c] = e4m3(x[r,c] * (448 / amax_r))
 // (round to nearest even, saturating); an all-zero row gets scale 1 and zeros.
 cudaError_t launch_quantize_rows_e4m3(const void* x, void* q, float* scale, int64_t rows,
@@ -85,7 +102,7 @@ cudaError_t launch_ep_regroup(const void* from, void* to, const int32_t* counts,
 // Expert-parallel exchange over peer memory (ep_p2p.cu).
 constexpr int kEpP2pMaxRanks = 8;
 enum EpP2pOp { kEpP2pCounts = 0, kEpP2pSend = 1, kEpP2pWaitRows = 2, kEpP2pReturn = 3,
-               kEpP2pWaitReturn = 4 };
+               kEpP2pWaitReturn = 4, kEpP2pSendLocal = 5, kEpP2pSendRemote = 6 };
 int64_t ep_p2p_region_bytes(int ranks, int experts, int64_t hidden, int64_t grouped_rows,
                             int64_t back_rows);
 int64_t ep_p2p_region_offset(int ranks, int experts, int64_t hidden, int64_t grouped_rows,
@@ -96,6 +113,12 @@ cudaError_t launch_ep_p2p(int op, const void* rows, const int32_t* aux, void* co
                           int64_t hidden, int64_t grouped_rows, int64_t back_rows,
                           int64_t timeout_ms, cudaStream_t stream);
 cudaError_t read_ep_status(int32_t* code, bool clear);
+// The gate/up GEMM (+ SwiGLU) of the P2P step on this rank's grouped rows,
+// taking each tile once the rows it needs have arrived (GemmArrival).
+cudaError_t launch_ep_p2p_gate_up(const void* gate_up, void* activated, void* const* regions,
+                                  int32_t* state, int ranks, int me, int experts, int64_t hidden,
+                                  int64_t intermediate, int64_t grouped_rows, int64_t back_rows,
+                                  int64_t timeout_ms, cudaStream_t stream, const char** error);
 cudaError_t launch_ep_p2p_down_return(const void* activated, const void* down, void* const* regions,
                                       int32_t* state, int ranks, int me, int experts,
                                       int64_t hidden, int64_t intermediate, int64_t grouped_rows,

@@ -185,6 +185,14 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     out one row per lane; at the expert-parallel configuration the separate,
     coalesced copy is faster, so it is off by default.
 
+    overlap=True (p2p with micro_batches=1, the default there) overlaps the row
+    exchange with the gate/up GEMM: this rank's own rows are copied first, the
+    other ranks' rows go out on a second stream, and the GEMM
+    (moe_ep_p2p_gate_up) takes each expert's tiles in the order their rows
+    arrive, waiting on a peer's rows flag before a tile that needs them.
+    Inside an expert the grouped rows follow that arrival order; GEMM rows are
+    independent, so the output bits do not change.
+
     micro_batches=m (p2p only) splits the local tokens into m consecutive
     slices, each with its own exchange region, run on their own streams in a
     pipeline: slice i sends its rows once slice i-1's rows have arrived (so the
@@ -196,7 +204,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
 
     def __init__(self, config, router_weight, gate_up, down, *, group=None, device="cuda",
                  routing_bias=None, backend=None, timeout_ms=10000, fused_return=False,
-                 micro_batches=1):
+                 micro_batches=1, overlap=None):
         super().__init__()
         self.config = config if isinstance(config, MoEConfig) else MoEConfig(*config)
         self.group = group
@@ -232,6 +240,11 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self.micro_batches = int(micro_batches)
         if self.micro_batches < 1 or (self.micro_batches > 1 and backend != "p2p"):
             raise ValueError("micro_batches must be 1, or >= 1 with the p2p backend")
+        if overlap is None:
+            overlap = backend == "p2p" and self.micro_batches == 1
+        if overlap and (backend != "p2p" or self.micro_batches != 1):
+            raise ValueError("overlap needs the p2p backend and micro_batches=1")
+        self.overlap = bool(overlap)
         self._lanes = [_Lane() for _ in range(self.micro_batches)]
         self._outputs = {}
         self._last_key = None
@@ -301,7 +314,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     @torch.inference_mode()
     def forward(self, x, events=None, out=None):
         """`events`, if given, maps stage names ("exchange", "gemm1", "gemm2",
-        "return") to (start, end) CUDA events recorded around those stages.
+        "return", and with overlap "send": the other ranks' rows, on the side
+        stream) to (start, end) CUDA events recorded around those stages.
         `out`, if given, receives the combined rows instead of the workspace's
         reusable output view."""
         cfg = self.config
@@ -442,16 +456,41 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         self._p2p(0, None, transport.counts, ex)
         if after_received is not None:
             stream.wait_event(after_received)
-        mark("exchange", 0)
-        self._p2p(1, transport.packed, transport.offsets, ex)
-        self._p2p(2, None, None, ex)
-        mark("exchange", 1)
+        sent = None
+        if self.overlap:
+            # other ranks' rows on the side stream, beside this rank's GEMM
+            if lane.stream is None:
+                lane.stream = torch.cuda.Stream(device=x.device)
+            counted = torch.cuda.Event()
+            counted.record(stream)
+            lane.stream.wait_event(counted)
+            with torch.cuda.stream(lane.stream):
+                mark("send", 0)
+                self._p2p(6, transport.packed, transport.offsets, ex)
+                mark("send", 1)
+                sent = torch.cuda.Event()
+                sent.record(lane.stream)
+            mark("exchange", 0)
+            self._p2p(5, transport.packed, transport.offsets, ex)
+            mark("exchange", 1)
+        else:
+            mark("exchange", 0)
+            self._p2p(1, transport.packed, transport.offsets, ex)
+            self._p2p(2, None, None, ex)
+            mark("exchange", 1)
         received = torch.cuda.Event()
         received.record(stream)
         if after_gemm is not None:
             stream.wait_event(after_gemm)
         mark("gemm1", 0)
-        ext.grouped_gemm_swiglu_out(ex.grouped, self.gate_up_weight, ex.offsets, activated)
+        if self.overlap:
+            experts, hidden, grouped_rows, back_rows = ex.shape
+            ext._call(ex.state.device, ext.lib.moe_ep_p2p_gate_up, self.gate_up_weight.data_ptr(),
+                      activated.data_ptr(), ctypes.addressof(ex.regions), ex.state.data_ptr(),
+                      self.ranks, self.rank, experts, hidden, cfg.intermediate, grouped_rows,
+                      back_rows, self.timeout_ms)
+        else:
+            ext.grouped_gemm_swiglu_out(ex.grouped, self.gate_up_weight, ex.offsets, activated)
         mark("gemm1", 1)
         mark("gemm2", 0)
         if self.fused_return:
@@ -474,6 +513,8 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             self._p2p(3, expert_out, None, ex)
         self._p2p(4, None, None, ex)
         mark("return", 1)
+        if sent is not None:
+            stream.wait_event(sent)
         if tokens:
             result = transport.combine(ex.back[:n], weights, out)
         else:

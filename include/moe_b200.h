@@ -246,13 +246,37 @@ int64_t moe_ep_p2p_state_words(int32_t ranks, int32_t experts);
  *   2 wait until every rank's rows arrived;
  *   3 return rows: rows = this rank's expert outputs in grouped order; each
  *     row goes back to its source's returned rows at its packed position;
- *   4 wait until every rank's results came back.
+ *   4 wait until every rank's results came back;
+ *   5 send local rows: op 1 for the rows of this rank's own experts only (an
+ *     HBM copy, no flag: the launches after it on the stream see them);
+ *   6 send remote rows: op 1 for the other ranks' rows; the rows flag of this
+ *     source is raised on each owner as soon as that owner's rows are stored
+ *     (at once on owners it sends nothing, and on this rank), so owners can
+ *     start on them while it still sends to others.  Runs beside the gate/up
+ *     GEMM of moe_ep_p2p_gate_up, on another stream.
+ * Inside an expert's grouped span the sources' rows follow their arrival
+ * order on the owner o: o's own rows, then those of o-1, o-2, ... (mod P).
  * Waits give up after timeout_ms, record status 2 (read by
  * moe_device_status) and return; capacity overflows record status 3. */
 int moe_ep_p2p(int32_t op, const void* rows, const int32_t* aux, void* const* regions,
                int32_t* state, int32_t ranks, int32_t rank, int32_t experts, int32_t alignment,
                int64_t hidden, int64_t grouped_rows, int64_t back_rows, int64_t timeout_ms,
                void* stream);
+
+/* The gate/up GEMM (+ SwiGLU) of the P2P expert-parallel step, overlapped
+ * with the row exchange (no counterpart in the reference, which is
+ * single-GPU; replaces op 2 + moe_grouped_gemm_swiglu on the grouped rows):
+ * activated [grouped_rows, intermediate] = swiglu(grouped rows x this rank's
+ * gate_up [E_l, 2*intermediate, hidden]).  It takes the tiles of each expert
+ * in arrival order -- first those of this rank's own rows (op 5, before it on
+ * the stream), then, source by source, those whose rows have arrived (ops 6
+ * of the other ranks): before a tile's first load the producer waits on the
+ * rows flags it needs (bounded by timeout_ms; status 6).  The same bits as
+ * moe_grouped_gemm_swiglu on the same rows. */
+int moe_ep_p2p_gate_up(const void* gate_up, void* activated, void* const* regions, int32_t* state,
+                       int32_t ranks, int32_t rank, int32_t experts, int64_t hidden,
+                       int64_t intermediate, int64_t grouped_rows, int64_t back_rows,
+                       int64_t timeout_ms, void* stream);
 
 /* The down GEMM of the P2P expert-parallel step fused with the return
  * exchange (replaces moe_grouped_gemm + op 3 of moe_ep_p2p): tcgen05 grouped
@@ -273,7 +297,8 @@ int moe_ep_p2p_down_return(const void* activated, const void* down, void* const*
  * expert-parallel capacity overflow, 4 a router copy wait, 5 two grouped-GEMM
  * launches that shared one tile-claim slot at the same time (one captured
  * graph replayed on two streams at once, or more than 512 captured GEMM
- * launches in flight together); their results are void. */
+ * launches in flight together); their results are void; 6 a gate/up GEMM of
+ * moe_ep_p2p_gate_up that gave up waiting for a peer's rows. */
 int moe_device_status(int32_t* code, int32_t clear);
 
 #ifdef __cplusplus

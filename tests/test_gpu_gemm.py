@@ -167,7 +167,9 @@ def test_tile_kinds_give_identical_bits(ext, tile, monkeypatch, swiglu):
     than one GPU running all experts)."""
     if tile != "single":
         pytest.skip("compares all kinds once")
-    a, w, offsets = make_problem([300, 0, 17, 129, 640, 5], 448, 2 * 192, seed=11)
+    # spans 304, 0, 24, 136, 640, 8 and 264: last pair tiles of 48, 24, 136,
+    # 128, 8 and 8 rows
+    a, w, offsets = make_problem([300, 0, 17, 129, 640, 5, 257], 448, 2 * 192, seed=11)
     results = {}
     for kind in TILES:
         monkeypatch.setenv("MOE_B200_GEMM_TILE", kind)
