@@ -462,9 +462,11 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
     constexpr int kStageK = stage_k<kFp8>();
     const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
+    pdl_trigger();  // the next kernel may launch and run its prologue
 
     // m-tile table (warp 0).
     if (warp == 0) {
+        pdl_wait();  // offsets and rows come from the kernels before this launch
         build_tile_table<kBM>(p, lane, mt_prefix, offs, tbase);
     } else if (warp == 1) {
         if (lane == 0) {
@@ -490,6 +492,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    if (warp != 0) pdl_wait();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -867,9 +870,11 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     constexpr int kStageK = stage_k<kFp8>();
     const int k_blocks = (p.k_dim + kStageK - 1) / kStageK;
     if (threadIdx.x == 32) enter_schedule(p.sched);
+    pdl_trigger();  // the next kernel may launch and run its prologue
 
     // m-tile table of 256-row tiles (warp 0, both CTAs).
     if (warp == 0) {
+        pdl_wait();  // offsets and rows come from the kernels before this launch
         build_tile_table<kPairBM>(p, lane, mt_prefix, offs, tbase);
     } else if (warp == 1) {
         if (lane == 0) {
@@ -897,6 +902,7 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                      "r"(kTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
     }
+    if (warp != 0) pdl_wait();
     tc_fence_before();
     cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
     tc_fence_after();
@@ -1266,16 +1272,19 @@ cudaError_t launch_pair(Kernel kernel, int smem_bytes, bool& configured, int& re
                         int sms, int64_t max_tiles, const CUtensorMap& map_a, const CUtensorMap& map_b,
                         const GemmParams& p, cudaStream_t stream, const GemmScatter& scatter = {}) {
     cudaLaunchConfig_t config = {};
-    cudaLaunchAttribute attribute[1];
+    cudaLaunchAttribute attribute[2];
     attribute[0].id = cudaLaunchAttributeClusterDimension;
     attribute[0].val.clusterDim.x = 2;
     attribute[0].val.clusterDim.y = 1;
     attribute[0].val.clusterDim.z = 1;
+    // a dependent launch of the kernel before it (see pdl_wait)
+    attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attribute[1].val.programmaticStreamSerializationAllowed = 1;
     config.blockDim = dim3(kThreads);
     config.dynamicSmemBytes = smem_bytes;
     config.stream = stream;
     config.attrs = attribute;
-    config.numAttrs = 1;
+    config.numAttrs = 2;
     if (!configured) {
         MOE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           smem_bytes));
@@ -1358,8 +1367,8 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     const int64_t max_tiles = ((rows + kBM - 1) / kBM + experts) * static_cast<int64_t>(p.n_tiles);
     const int grid = static_cast<int>(max_tiles < info.sms ? max_tiles : info.sms);
     const GemmScatter none = {};
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, none);
-    return cudaGetLastError();
+    return launch_dependent(kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, map_a, map_b, p,
+                            none);
 }
 
 cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int32_t* offsets,
@@ -1416,8 +1425,8 @@ cudaError_t launch_grouped_gemm_scatter(const void* a, const void* b, const int3
                            pair_configured[device & 63], resident[device & 63], info.sms, INT64_MAX,
                            map_a, map_b, p, stream, scatter);
     }
-    kernel<<<info.sms, kThreads, kSmemBytes, stream>>>(map_a, map_b, p, scatter);
-    return cudaGetLastError();
+    return launch_dependent(kernel, dim3(info.sms), dim3(kThreads), kSmemBytes, stream, map_a, map_b,
+                            p, scatter);
 }
 
 bool grouped_gemm_uses_pair(int64_t rows, int experts) {

@@ -72,6 +72,7 @@ router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
     const int tx = tid % R::kTx, ty = tid / R::kTx;
     const int64_t t0 = static_cast<int64_t>(blockIdx.x) * TT;
     const int e0 = blockIdx.y * TE;
+    pdl_trigger();  // the top-k kernel may launch; it waits for these logits
 
     uint4 xr[R::kXPieces];
     float4 wr[R::kWPieces];
@@ -359,6 +360,7 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunks = (hidden + R::kChunk - 1) / R::kChunk;
     const int64_t blocks = (tokens + R::kBlockTokens - 1) / R::kBlockTokens;
+    pdl_trigger();  // the dispatch index kernel may launch; it waits for these ids
     if (threadIdx.x == 0) {
         for (int s = 0; s < R::kStages; ++s) {
             bar_init(&full[s], 1);
@@ -492,6 +494,8 @@ topk_softmax_kernel(const float* __restrict__ logits, const float* __restrict__ 
                     float* __restrict__ weights, int64_t tokens, int experts, int topk) {
     const int lane = threadIdx.x & 31;
     const int64_t token = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    pdl_trigger();
+    pdl_wait();  // a dependent launch of the logits kernel
     if (token >= tokens) return;  // uniform per warp
 
     float v[VPL];
@@ -611,14 +615,13 @@ cudaError_t launch_topk(const float* logits, const float* bias, int32_t* ids32, 
     if (tokens == 0) return cudaSuccess;
     const unsigned blocks = static_cast<unsigned>((tokens + 7) / 8);
     if (experts <= 32)
-        topk_softmax_kernel<1><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+        return launch_dependent(topk_softmax_kernel<1>, dim3(blocks), dim3(256), 0, stream, logits, bias, ids32, ids64, weights, tokens, experts, topk);
     else if (experts <= 64)
-        topk_softmax_kernel<2><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+        return launch_dependent(topk_softmax_kernel<2>, dim3(blocks), dim3(256), 0, stream, logits, bias, ids32, ids64, weights, tokens, experts, topk);
     else if (experts <= 128)
-        topk_softmax_kernel<4><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
+        return launch_dependent(topk_softmax_kernel<4>, dim3(blocks), dim3(256), 0, stream, logits, bias, ids32, ids64, weights, tokens, experts, topk);
     else
-        topk_softmax_kernel<8><<<blocks, 256, 0, stream>>>(logits, bias, ids32, ids64, weights, tokens, experts, topk);
-    return cudaGetLastError();
+        return launch_dependent(topk_softmax_kernel<8>, dim3(blocks), dim3(256), 0, stream, logits, bias, ids32, ids64, weights, tokens, experts, topk);
 }
 
 }  // namespace moe

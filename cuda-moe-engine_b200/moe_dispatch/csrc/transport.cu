@@ -45,9 +45,10 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The pack kernel may start now: it reads its token rows, then waits for
     // this grid (griddepcontrol.wait) before it needs anything computed here.
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    pdl_trigger();
     for (int i = tid; i < 32 * experts; i += kIndexThreads) hist[i] = 0;
     for (int i = tid; i < experts; i += kIndexThreads) running[i] = 0;
+    pdl_wait();  // the ids come from the kernel before (the router)
     __syncthreads();
 
     const int64_t chunk0 = static_cast<int64_t>(blockIdx.x) * kDispatchChunk;
@@ -160,6 +161,7 @@ pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
     __shared__ int64_t dest[kMaxTopk];
     const int64_t t = blockIdx.x;
     constexpr int kUnroll = 4;
+    pdl_trigger();  // the grouped GEMM may launch and run its prologue
     // Launched as a programmatic dependent of the index kernel: the first
     // slice of this token's row does not depend on it, so load it first.
     V first[kUnroll];
@@ -170,7 +172,7 @@ pack_kernel(const V* __restrict__ x, const int32_t* __restrict__ ids,
             if (c < row_vecs) first[u] = __ldg(x + t * row_vecs + c);
         }
     }
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    pdl_wait();
     if (t < tokens) {
         if (threadIdx.x < topk) {
             const int64_t p = t * topk + threadIdx.x;
@@ -237,6 +239,7 @@ combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __re
     __shared__ int64_t rows[kMaxTopk];
     __shared__ float ws[kMaxTopk];
     const int64_t t = blockIdx.x;
+    pdl_wait();  // a dependent launch of the down GEMM
     if (threadIdx.x < topk) {
         const int64_t p = t * topk + threadIdx.x;
         const int32_t r = inverse[p];
@@ -348,15 +351,14 @@ cudaError_t launch_combine_t(const void* eo, const int32_t* inverse, const float
     // 256-thread CTAs: 512 (one vector per thread) measured slower, 29.7 vs 26.6 us
     // at top-2 and 62.4 vs 60 us at top-8 for 4096 rows of 8 KB.
     const int threads = row_vecs >= 256 ? 256 : 128;
+    const dim3 grid(static_cast<unsigned>(tokens));
     if (topk <= 2)
-        combine_kernel<DT, VB, 2><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
-            static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
-            row_vecs, packed_rows);
-    else
-        combine_kernel<DT, VB, 8><<<static_cast<unsigned>(tokens), threads, 0, stream>>>(
-            static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output), tokens, topk,
-            row_vecs, packed_rows);
-    return cudaGetLastError();
+        return launch_dependent(combine_kernel<DT, VB, 2>, grid, dim3(threads), 0, stream,
+                                static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output),
+                                tokens, topk, row_vecs, packed_rows);
+    return launch_dependent(combine_kernel<DT, VB, 8>, grid, dim3(threads), 0, stream,
+                            static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output),
+                            tokens, topk, row_vecs, packed_rows);
 }
 
 template <int DT>
@@ -423,9 +425,9 @@ cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_
                                           65 * kMaxDispatchExperts * static_cast<int>(sizeof(int32_t))));
         configured[device & 63] = true;
     }
-    dispatch_index_kernel<<<static_cast<unsigned>(chunks), kIndexThreads, smem, stream>>>(
-        ids, n, experts, alignment, counts, offsets, slots, scratch);
-    MOE_CUDA_TRY(cudaGetLastError());
+    MOE_CUDA_TRY(launch_dependent(dispatch_index_kernel, dim3(static_cast<unsigned>(chunks)),
+                                  dim3(kIndexThreads), smem, stream, ids, n, experts, alignment,
+                                  counts, offsets, slots, scratch));
     const int32_t* table = scratch + kScratchHeader;
     const int64_t row_bytes = hidden * dtype_bytes(dtype);
     switch (vector_bytes) {

@@ -16,9 +16,11 @@ expert-parallel layer the north star asks for.  Rank r of P owns experts
   8. return them to their source ranks                   (all_to_all_single)
   9. weighted combine at the source                      (moe_combine)
 
-Inside an expert, received rows are ordered by source rank, and ranks hold
-consecutive token ranges, so the grouped rows are exactly the rows a single GPU
-would pack: the output is bit-identical to MoEBlock on one GPU.
+Each grouped row is computed on its own (GEMM rows are independent), so the
+output is bit-identical to MoEBlock on one GPU whatever the order of the rows
+inside an expert: source-major on the NCCL path (ranks hold consecutive token
+ranges, so these are the rows a single GPU would pack), arrival order on the
+P2P path.
 
 Two exchange backends:
 
@@ -26,8 +28,11 @@ Two exchange backends:
   region of its HBM with the others through CUDA IPC.  Counts go out with peer
   stores and flags, senders write rows straight into the owners' expert-major
   buffers and owners write results straight back into the sources' packed
-  slots (``moe_ep_p2p``).  No host synchronisation: the whole step can be
-  captured in a CUDA graph.  Waits on peers are bounded and report through
+  slots (``moe_ep_p2p``).  The exchange runs beside the gate/up GEMM, which
+  takes each expert's tiles in the order their rows arrive
+  (``moe_ep_p2p_gate_up``), and the down GEMM returns the rows itself
+  (``moe_ep_p2p_down_return``).  No host synchronisation: the whole step can
+  be captured in a CUDA graph.  Waits on peers are bounded and report through
   ``moe_device_status``.
 * ``"nccl"``: steps 3-4 and 8 as ``all_to_all_single`` with the split sizes
   read on the host (one synchronisation per forward), and the regroup kernels.
@@ -179,11 +184,14 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     [E_l, 2I, H] and down [E_l, H, I] are this rank's experts.  forward(x) takes
     this rank's tokens x [T_l, H] bf16 and returns their outputs [T_l, H].
 
-    fused_return=True (p2p only) runs the down GEMM with an epilogue that
-    stores each result row straight into its source rank's slot
-    (moe_ep_p2p_down_return) instead of a separate return copy.  Its stores go
-    out one row per lane; at the expert-parallel configuration the separate,
-    coalesced copy is faster, so it is off by default.
+    fused_return=True (p2p only; the default there) runs the down GEMM with an
+    epilogue that stores each result row straight into its source rank's slot
+    (moe_ep_p2p_down_return) instead of a separate return copy, so the return
+    crosses NVLink while the GEMM runs.  With the CTA-pair tile the epilogue
+    stages each 32 x 32 chunk in shared memory and stores 64-byte row
+    segments.  Measured on two B200s: the return stage falls from 2.19 to
+    0.40 ms at the E=256 configuration and from 0.157 to 0.080 ms at the
+    Mixtral shape, the down GEMM slows by 0.14 and 0.015 ms.
 
     overlap=True (p2p with micro_batches=1, the default there) overlaps the row
     exchange with the gate/up GEMM: this rank's own rows are copied first, the
@@ -203,7 +211,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     """
 
     def __init__(self, config, router_weight, gate_up, down, *, group=None, device="cuda",
-                 routing_bias=None, backend=None, timeout_ms=10000, fused_return=False,
+                 routing_bias=None, backend=None, timeout_ms=10000, fused_return=None,
                  micro_batches=1, overlap=None):
         super().__init__()
         self.config = config if isinstance(config, MoEConfig) else MoEConfig(*config)
@@ -236,6 +244,10 @@ class ExpertParallelMoEBlock(torch.nn.Module):
             raise ValueError("backend must be p2p or nccl")
         self.backend = backend
         self.timeout_ms = int(timeout_ms)
+        if fused_return is None:
+            fused_return = backend == "p2p"
+        if fused_return and backend != "p2p":
+            raise ValueError("fused_return needs the p2p backend")
         self.fused_return = bool(fused_return)
         self.micro_batches = int(micro_batches)
         if self.micro_batches < 1 or (self.micro_batches > 1 and backend != "p2p"):
