@@ -331,9 +331,9 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 // leaves every logit in every lane, and lane e then holds expert e's biased
 // score for the warp top-k.  The copies stream every token row from HBM once
 // and put each weight chunk in shared memory once per block of tokens.
-template <int EMAX, int TW, int JC, int STAGES>
+template <int EMAX, int TW, int JC, int STAGES, int WARPS = 8>
 struct StagedRouter {
-    static constexpr int kWarps = 8;  // compute warps; one more issues the copies
+    static constexpr int kWarps = WARPS;  // compute warps; one more issues the copies
     static constexpr int kThreads = 32 * (kWarps + 1);
     static constexpr int kBlockTokens = kWarps * TW;
     static constexpr int kChunk = 256 * JC;  // hidden elements per stage
@@ -344,14 +344,17 @@ struct StagedRouter {
     static constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 16;
 };
 
-template <int EMAX, int TW, int JC, int STAGES>
-__global__ void __launch_bounds__(StagedRouter<EMAX, TW, JC, STAGES>::kThreads, 1)
+template <int EMAX, int TW, int JC, int STAGES, int WARPS>
+__global__ void __launch_bounds__(StagedRouter<EMAX, TW, JC, STAGES, WARPS>::kThreads, 1)
 router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                      const float* __restrict__ bias, float* __restrict__ logits,
                      int32_t* __restrict__ ids32, int64_t* __restrict__ ids64,
                      float* __restrict__ weights, int64_t tokens, int hidden, int experts,
-                     int topk) {
-    using R = StagedRouter<EMAX, TW, JC, STAGES>;
+                     int topk, int block_tokens) {
+    // block_tokens (a multiple of TW, at most kBlockTokens): tokens per block,
+    // so that small batches spread over every SM; warps past it idle through
+    // the block (their results are not written).
+    using R = StagedRouter<EMAX, TW, JC, STAGES, WARPS>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + R::kStages * R::kStageBytes);
     uint64_t* empty = full + R::kStages;
@@ -359,7 +362,7 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunks = (hidden + R::kChunk - 1) / R::kChunk;
-    const int64_t blocks = (tokens + R::kBlockTokens - 1) / R::kBlockTokens;
+    const int64_t blocks = (tokens + block_tokens - 1) / block_tokens;
     pdl_trigger();  // the dispatch index kernel may launch; it waits for these ids
     if (threadIdx.x == 0) {
         for (int s = 0; s < R::kStages; ++s) {
@@ -377,8 +380,8 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
         int stage = 0;
         uint32_t phase = 0, armed = 0, last_parity = 0;
         for (int64_t b = blockIdx.x; b < blocks && !*abort_flag; b += gridDim.x) {
-            const int64_t t0 = b * R::kBlockTokens;
-            const int nt = static_cast<int>(tokens - t0 < R::kBlockTokens ? tokens - t0 : R::kBlockTokens);
+            const int64_t t0 = b * block_tokens;
+            const int nt = static_cast<int>(tokens - t0 < block_tokens ? tokens - t0 : block_tokens);
             for (int c = 0; c < chunks; ++c) {
                 if (!bar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
                 const int h0 = c * R::kChunk;
@@ -412,7 +415,9 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     int stage = 0;
     uint32_t phase = 0;
     for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x) {
-        const int64_t t0 = b * R::kBlockTokens + warp * TW;
+        const int64_t t0 = b * block_tokens + warp * TW;
+        // this block's tokens, and how many of them belong to this warp
+        const int64_t block_end = (b + 1) * block_tokens < tokens ? (b + 1) * block_tokens : tokens;
         float acc[TW][EMAX];
 #pragma unroll
         for (int i = 0; i < TW; ++i)
@@ -431,7 +436,7 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
 #pragma unroll
                 for (int i = 0; i < TW; ++i) {
                     uint4 raw = make_uint4(0, 0, 0, 0);
-                    if (t0 + i < tokens)
+                    if (t0 + i < block_end)
                         raw = *reinterpret_cast<const uint4*>(xs + ((warp * TW + i) * R::kChunk + hl) * 2);
                     const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
@@ -469,7 +474,7 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
 #pragma unroll
         for (int i = 0; i < TW; ++i) {
             const int64_t t = t0 + i;
-            if (t >= tokens) break;  // uniform per warp
+            if (t >= block_end) break;  // uniform per warp
             float mine = 0.0f;
 #pragma unroll
             for (int e = 0; e < EMAX; ++e)
@@ -570,26 +575,36 @@ cudaError_t launch_router_logits(const void* x, const float* w, float* logits, i
     return launch_tiled<64, 64, 8, 4>(xb, w, logits, tokens, h, experts, stream);
 }
 
-template <int EMAX, int TW, int JC, int STAGES>
+template <int EMAX, int TW, int JC, int STAGES, int WARPS = 8>
 static cudaError_t launch_staged(const void* x, const float* w, const float* bias, float* logits,
                                  int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens,
                                  int64_t hidden, int experts, int topk, cudaStream_t stream) {
-    using R = StagedRouter<EMAX, TW, JC, STAGES>;
+    using R = StagedRouter<EMAX, TW, JC, STAGES, WARPS>;
     static int sms[64] = {};
     static bool configured[64] = {};
     int device = 0;
     MOE_CUDA_TRY(cudaGetDevice(&device));
     if (!configured[device & 63]) {
-        MOE_CUDA_TRY(cudaFuncSetAttribute(router_staged_kernel<EMAX, TW, JC, STAGES>,
+        MOE_CUDA_TRY(cudaFuncSetAttribute(router_staged_kernel<EMAX, TW, JC, STAGES, WARPS>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, R::kSmemBytes));
         MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[device & 63], cudaDevAttrMultiProcessorCount, device));
         configured[device & 63] = true;
     }
-    const int64_t blocks = (tokens + R::kBlockTokens - 1) / R::kBlockTokens;
-    const unsigned grid = static_cast<unsigned>(blocks < sms[device & 63] ? blocks : sms[device & 63]);
-    router_staged_kernel<EMAX, TW, JC, STAGES><<<grid, R::kThreads, R::kSmemBytes, stream>>>(
+    const int64_t sm = sms[device & 63];
+    // Full blocks once there are at least as many as SMs; below that, fewer
+    // tokens per block (a multiple of TW) so that every SM gets one.
+    int64_t block_tokens = R::kBlockTokens;
+    if (tokens < sm * R::kBlockTokens) {
+        block_tokens = ((tokens + sm - 1) / sm + TW - 1) / TW * TW;
+        if (block_tokens < TW) block_tokens = TW;
+    }
+    if (const char* env = getenv("MOE_B200_ROUTER_BLOCK_FULL"))  // tuning knob: full blocks
+        if (env[0] == '1') block_tokens = R::kBlockTokens;
+    const int64_t blocks = (tokens + block_tokens - 1) / block_tokens;
+    const unsigned grid = static_cast<unsigned>(blocks < sm ? blocks : sm);
+    router_staged_kernel<EMAX, TW, JC, STAGES, WARPS><<<grid, R::kThreads, R::kSmemBytes, stream>>>(
         static_cast<const __nv_bfloat16*>(x), w, bias, logits, ids32, ids64, weights, tokens,
-        static_cast<int>(hidden), experts, topk);
+        static_cast<int>(hidden), experts, topk, static_cast<int>(block_tokens));
     return cudaGetLastError();
 }
 
@@ -599,8 +614,13 @@ cudaError_t launch_route(const void* x, const float* w, const float* bias, float
     if (tokens == 0) return cudaSuccess;
     // Measured on B200 (Mixtral router, T=4096, H=4096, E=8): 1024-element
     // chunks in two stages 25.6 us; 512 in four 31.7 us; 256 in six 48.0 us.
-    if (experts <= 8)
+    if (experts <= 8) {
+        // tuning knob: 16 compute warps of 2 tokens instead of 8 of 4 (same bits)
+        const char* env = getenv("MOE_B200_ROUTER_WARPS");
+        if (env && atoi(env) == 16)
+            return launch_staged<8, 2, 4, 2, 16>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
         return launch_staged<8, 4, 4, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
+    }
     if (experts <= 16)
         return launch_staged<16, 2, 4, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
     if (experts <= kRouterSlicedMaxExperts)

@@ -21,25 +21,30 @@ import torch
 STAGES = ("router", "dispatch", "experts", "gemm1", "gemm2", "combine", "forward")
 
 
-def build(workload_name, device="cuda", tokens=None, experts=None):
-    """Block + input for a named workload, weights drawn on the GPU."""
+def build(workload_name, device="cuda", tokens=None, experts=None, intermediate=None):
+    """Block + input for a named workload: the workload's router and routing
+    bias (so the expert loads are skewed as in the benchmark), expert weights
+    and tokens drawn on the GPU."""
     from .layer import MoEBlock, MoEConfig, MoEWeights
-    from .routing import WORKLOADS
+    from .routing import WORKLOADS, block_router
 
     w = WORKLOADS[workload_name]
     tokens = tokens or w.tokens
     experts = experts or w.experts
-    cfg = MoEConfig(w.hidden, w.intermediate, experts, min(w.topk, experts))
+    inter = intermediate or w.intermediate  # a small one keeps router captures small
+    cfg = MoEConfig(w.hidden, inter, experts, min(w.topk, experts))
     g = torch.Generator(device=device).manual_seed(1000 + w.seed)
-    router = torch.randn(experts, w.hidden, device=device, generator=g) / w.hidden**0.5
-    gate_up = torch.empty(experts, 2 * w.intermediate, w.hidden, device=device, dtype=torch.bfloat16)
-    down = torch.empty(experts, w.hidden, w.intermediate, device=device, dtype=torch.bfloat16)
+    router, bias = block_router(w)
+    router, bias = router[:experts].to(device), bias[:experts]
+    gate_up = torch.empty(experts, 2 * inter, w.hidden, device=device, dtype=torch.bfloat16)
+    down = torch.empty(experts, w.hidden, inter, device=device, dtype=torch.bfloat16)
     for e in range(experts):
-        gate_up[e] = (torch.randn(2 * w.intermediate, w.hidden, device=device, generator=g)
+        gate_up[e] = (torch.randn(2 * inter, w.hidden, device=device, generator=g)
                       / w.hidden**0.5).to(torch.bfloat16)
-        down[e] = (torch.randn(w.hidden, w.intermediate, device=device, generator=g)
-                   / w.intermediate**0.5).to(torch.bfloat16)
+        down[e] = (torch.randn(w.hidden, inter, device=device, generator=g)
+                   / inter**0.5).to(torch.bfloat16)
     block = MoEBlock(cfg, device=device, weights=MoEWeights(router, gate_up, down))
+    block.routing_bias.copy_(bias)
     x = torch.randn(tokens, w.hidden, device=device, generator=g).to(torch.bfloat16)
     return block, x
 
@@ -164,6 +169,8 @@ def main():
     parser.add_argument("--iters", type=int, default=2)
     parser.add_argument("--tokens", type=int, default=None)
     parser.add_argument("--experts", type=int, default=None)
+    parser.add_argument("--intermediate", type=int, default=None,
+                        help="override the expert width (router captures need no real experts)")
     parser.add_argument("--trace", default=None)
     parser.add_argument("--transport", action="store_true",
                         help="time dispatch and combine at the transport-only configuration")
@@ -172,7 +179,8 @@ def main():
     if args.transport or args.transport_stage:
         transport_sweep(stage=args.transport_stage, iters=args.iters)
         return 0
-    block, x = build(args.workload, tokens=args.tokens, experts=args.experts)
+    block, x = build(args.workload, tokens=args.tokens, experts=args.experts,
+                     intermediate=args.intermediate)
     if args.trace:
         print(export_trace(block, x, args.trace))
         return 0
