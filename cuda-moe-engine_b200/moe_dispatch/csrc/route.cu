@@ -414,15 +414,17 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     // -------------------------------------------------------- compute warps
     int stage = 0;
     uint32_t phase = 0;
+    static_assert(EMAX % 8 == 0, "experts are loaded in groups of 8");
     for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x) {
         const int64_t t0 = b * block_tokens + warp * TW;
         // this block's tokens, and how many of them belong to this warp
         const int64_t block_end = (b + 1) * block_tokens < tokens ? (b + 1) * block_tokens : tokens;
-        float acc[TW][EMAX];
+        // acc2[i][q] holds the logits of experts 2q and 2q+1 for token i
+        float2 acc2[TW][EMAX / 2];
 #pragma unroll
         for (int i = 0; i < TW; ++i)
 #pragma unroll
-            for (int e = 0; e < EMAX; ++e) acc[i][e] = 0.0f;
+            for (int q = 0; q < EMAX / 2; ++q) acc2[i][q] = make_float2(0.0f, 0.0f);
         for (int c = 0; c < chunks; ++c) {
             if (!bar_wait(&full[stage], phase, abort_flag)) return;
             const uint8_t* xs = smem + stage * R::kStageBytes;
@@ -445,16 +447,33 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
                         xv[i][2 * q + 1] = bf16_bits_to_f32(words[q] >> 16);
                     }
                 }
+                // Eight experts' weights are loaded together, then j-outer and
+                // expert-inner packed FMAs (__ffma2_rn: two round-to-nearest
+                // fmaf) give TW * 4 independent chains, where expert-outer
+                // order left 4 dependent chains between shared-memory loads.
+                // Every logit still takes its FMAs in increasing h.  Rows of
+                // experts past `experts` hold stale shared memory; their sums
+                // are never selected.
 #pragma unroll
-                for (int e = 0; e < EMAX; ++e) {
-                    if (e >= experts) break;
-                    const float4* wr = reinterpret_cast<const float4*>(ws + (e * R::kChunk + hl) * 4);
-                    const float4 w0 = wr[0], w1 = wr[1];
-                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+                for (int eg = 0; eg < EMAX; eg += 8) {
+                    float wv[8][8];
 #pragma unroll
-                    for (int i = 0; i < TW; ++i)
+                    for (int e = 0; e < 8; ++e) {
+                        const float4* wr =
+                            reinterpret_cast<const float4*>(ws + ((eg + e) * R::kChunk + hl) * 4);
+                        const float4 w0 = wr[0], w1 = wr[1];
+                        wv[e][0] = w0.x; wv[e][1] = w0.y; wv[e][2] = w0.z; wv[e][3] = w0.w;
+                        wv[e][4] = w1.x; wv[e][5] = w1.y; wv[e][6] = w1.z; wv[e][7] = w1.w;
+                    }
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) acc[i][e] = fmaf(xv[i][j], wv[j], acc[i][e]);
+                    for (int j = 0; j < 8; ++j)
+#pragma unroll
+                        for (int e = 0; e < 8; e += 2)
+#pragma unroll
+                            for (int i = 0; i < TW; ++i)
+                                acc2[i][(eg + e) / 2] =
+                                    __ffma2_rn(make_float2(xv[i][j], xv[i][j]),
+                                               make_float2(wv[e][j], wv[e + 1][j]), acc2[i][(eg + e) / 2]);
                 }
             }
             __syncwarp();
@@ -464,6 +483,14 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
                 phase ^= 1u;
             }
         }
+        float acc[TW][EMAX];
+#pragma unroll
+        for (int i = 0; i < TW; ++i)
+#pragma unroll
+            for (int q = 0; q < EMAX / 2; ++q) {
+                acc[i][2 * q] = acc2[i][q].x;
+                acc[i][2 * q + 1] = acc2[i][q].y;
+            }
 #pragma unroll
         for (int i = 0; i < TW; ++i)
 #pragma unroll

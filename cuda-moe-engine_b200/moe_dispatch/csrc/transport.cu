@@ -280,6 +280,64 @@ combine_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __re
     }
 }
 
+// combine for top-k <= 2: each thread takes CU columns of the token and issues
+// the loads of all of them (2 * CU vectors) before the first add, instead of
+// two per column; same products and the same k-ordered adds as combine_kernel.
+template <int DT, int VB, int CU>
+__global__ void __launch_bounds__(256)
+combine_top2_kernel(const typename VecOf<VB>::T* __restrict__ eo, const int32_t* __restrict__ inverse,
+                    const float* __restrict__ weights, typename VecOf<VB>::T* __restrict__ out,
+                    int64_t tokens, int topk, int64_t row_vecs, int64_t packed_rows) {
+    using V = typename VecOf<VB>::T;
+    using E = Elem<DT>;
+    using T = typename E::T;
+    constexpr int N = VB / sizeof(T);
+    union Pun {
+        V v;
+        T e[N];
+    };
+    const int64_t t = blockIdx.x;
+    pdl_wait();  // a dependent launch of the down GEMM
+    int64_t row[2];
+    float w[2];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int64_t p = t * topk + j;
+        const int32_t r = j < topk ? __ldg(inverse + p) : -1;
+        row[j] = (r >= 0 && r < packed_rows) ? r : -1;
+        w[j] = j < topk ? __ldg(weights + p) : 0.0f;
+    }
+    for (int64_t c0 = threadIdx.x; c0 < row_vecs; c0 += static_cast<int64_t>(blockDim.x) * CU) {
+        Pun in[CU][2];
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+            const int64_t c = c0 + u * blockDim.x;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (row[j] >= 0 && c < row_vecs) in[u][j].v = __ldg(eo + row[j] * row_vecs + c);
+        }
+#pragma unroll
+        for (int u = 0; u < CU; ++u) {
+            const int64_t c = c0 + u * blockDim.x;
+            if (c >= row_vecs) break;
+            float acc[N];
+#pragma unroll
+            for (int i = 0; i < N; ++i) acc[i] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                if (row[j] < 0) continue;
+#pragma unroll
+                for (int i = 0; i < N; ++i)
+                    acc[i] = __fadd_rn(acc[i], __fmul_rn(w[j], E::load(in[u][j].e[i])));
+            }
+            Pun o;
+#pragma unroll
+            for (int i = 0; i < N; ++i) o.e[i] = E::store(acc[i]);
+            out[t * row_vecs + c] = o.v;
+        }
+    }
+}
+
 // swiglu: out[r,c] = cast(silu(g) * u), g = f32(proj[r,c]), u = f32(proj[r,c+W]);
 // rows at or past *valid_rows are zero (dispatch.cu:277-292).
 template <int DT, int VB>
@@ -353,7 +411,7 @@ cudaError_t launch_combine_t(const void* eo, const int32_t* inverse, const float
     const int threads = row_vecs >= 256 ? 256 : 128;
     const dim3 grid(static_cast<unsigned>(tokens));
     if (topk <= 2)
-        return launch_dependent(combine_kernel<DT, VB, 2>, grid, dim3(threads), 0, stream,
+        return launch_dependent(combine_top2_kernel<DT, VB, 2>, grid, dim3(threads), 0, stream,
                                 static_cast<const V*>(eo), inverse, weights, static_cast<V*>(output),
                                 tokens, topk, row_vecs, packed_rows);
     return launch_dependent(combine_kernel<DT, VB, 8>, grid, dim3(threads), 0, stream,
