@@ -128,8 +128,7 @@ def parse_args(argv=None):
     parser.add_argument("--ep-micro-batches", type=int, default=1,
                         help="p2p only: token slices pipelined so exchanges overlap the GEMMs")
     parser.add_argument("--ep-overlap", type=int, choices=[0, 1], default=None,
-                        help="p2p: exchange beside the arrival-ordered gate/up GEMM (default on "
-                             "with one micro-batch)")
+                        help="p2p: exchange beside the arrival-ordered gate/up GEMM (default off)")
     parser.add_argument("--ep-fused-return", type=int, choices=[0, 1], default=None,
                         help="p2p: the down GEMM returns the rows itself (default: the block's)")
     parser.add_argument("--reference-gpu-worker", action="store_true", help=argparse.SUPPRESS)

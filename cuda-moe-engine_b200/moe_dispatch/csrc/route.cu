@@ -331,9 +331,9 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
 // leaves every logit in every lane, and lane e then holds expert e's biased
 // score for the warp top-k.  The copies stream every token row from HBM once
 // and put each weight chunk in shared memory once per block of tokens.
-template <int EMAX, int TW, int JC, int STAGES, int WARPS = 8>
+template <int EMAX, int TW, int JC, int STAGES>
 struct StagedRouter {
-    static constexpr int kWarps = WARPS;  // compute warps; one more issues the copies
+    static constexpr int kWarps = 8;  // compute warps; one more issues the copies
     static constexpr int kThreads = 32 * (kWarps + 1);
     static constexpr int kBlockTokens = kWarps * TW;
     static constexpr int kChunk = 256 * JC;  // hidden elements per stage
@@ -344,8 +344,8 @@ struct StagedRouter {
     static constexpr int kSmemBytes = kStages * kStageBytes + 2 * kStages * 8 + 16;
 };
 
-template <int EMAX, int TW, int JC, int STAGES, int WARPS>
-__global__ void __launch_bounds__(StagedRouter<EMAX, TW, JC, STAGES, WARPS>::kThreads, 1)
+template <int EMAX, int TW, int JC, int STAGES>
+__global__ void __launch_bounds__(StagedRouter<EMAX, TW, JC, STAGES>::kThreads, 1)
 router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
                      const float* __restrict__ bias, float* __restrict__ logits,
                      int32_t* __restrict__ ids32, int64_t* __restrict__ ids64,
@@ -354,7 +354,7 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     // block_tokens (a multiple of TW, at most kBlockTokens): tokens per block,
     // so that small batches spread over every SM; warps past it idle through
     // the block (their results are not written).
-    using R = StagedRouter<EMAX, TW, JC, STAGES, WARPS>;
+    using R = StagedRouter<EMAX, TW, JC, STAGES>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + R::kStages * R::kStageBytes);
     uint64_t* empty = full + R::kStages;
@@ -414,17 +414,15 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
     // -------------------------------------------------------- compute warps
     int stage = 0;
     uint32_t phase = 0;
-    static_assert(EMAX % 8 == 0, "experts are loaded in groups of 8");
     for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x) {
         const int64_t t0 = b * block_tokens + warp * TW;
         // this block's tokens, and how many of them belong to this warp
         const int64_t block_end = (b + 1) * block_tokens < tokens ? (b + 1) * block_tokens : tokens;
-        // acc2[i][q] holds the logits of experts 2q and 2q+1 for token i
-        float2 acc2[TW][EMAX / 2];
+        float acc[TW][EMAX];
 #pragma unroll
         for (int i = 0; i < TW; ++i)
 #pragma unroll
-            for (int q = 0; q < EMAX / 2; ++q) acc2[i][q] = make_float2(0.0f, 0.0f);
+            for (int e = 0; e < EMAX; ++e) acc[i][e] = 0.0f;
         for (int c = 0; c < chunks; ++c) {
             if (!bar_wait(&full[stage], phase, abort_flag)) return;
             const uint8_t* xs = smem + stage * R::kStageBytes;
@@ -447,33 +445,16 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
                         xv[i][2 * q + 1] = bf16_bits_to_f32(words[q] >> 16);
                     }
                 }
-                // Eight experts' weights are loaded together, then j-outer and
-                // expert-inner packed FMAs (__ffma2_rn: two round-to-nearest
-                // fmaf) give TW * 4 independent chains, where expert-outer
-                // order left 4 dependent chains between shared-memory loads.
-                // Every logit still takes its FMAs in increasing h.  Rows of
-                // experts past `experts` hold stale shared memory; their sums
-                // are never selected.
 #pragma unroll
-                for (int eg = 0; eg < EMAX; eg += 8) {
-                    float wv[8][8];
+                for (int e = 0; e < EMAX; ++e) {
+                    if (e >= experts) break;
+                    const float4* wr = reinterpret_cast<const float4*>(ws + (e * R::kChunk + hl) * 4);
+                    const float4 w0 = wr[0], w1 = wr[1];
+                    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        const float4* wr =
-                            reinterpret_cast<const float4*>(ws + ((eg + e) * R::kChunk + hl) * 4);
-                        const float4 w0 = wr[0], w1 = wr[1];
-                        wv[e][0] = w0.x; wv[e][1] = w0.y; wv[e][2] = w0.z; wv[e][3] = w0.w;
-                        wv[e][4] = w1.x; wv[e][5] = w1.y; wv[e][6] = w1.z; wv[e][7] = w1.w;
-                    }
+                    for (int i = 0; i < TW; ++i)
 #pragma unroll
-                    for (int j = 0; j < 8; ++j)
-#pragma unroll
-                        for (int e = 0; e < 8; e += 2)
-#pragma unroll
-                            for (int i = 0; i < TW; ++i)
-                                acc2[i][(eg + e) / 2] =
-                                    __ffma2_rn(make_float2(xv[i][j], xv[i][j]),
-                                               make_float2(wv[e][j], wv[e + 1][j]), acc2[i][(eg + e) / 2]);
+                        for (int j = 0; j < 8; ++j) acc[i][e] = fmaf(xv[i][j], wv[j], acc[i][e]);
                 }
             }
             __syncwarp();
@@ -483,14 +464,6 @@ router_staged_kernel(const __nv_bfloat16* __restrict__ x, const float* __restric
                 phase ^= 1u;
             }
         }
-        float acc[TW][EMAX];
-#pragma unroll
-        for (int i = 0; i < TW; ++i)
-#pragma unroll
-            for (int q = 0; q < EMAX / 2; ++q) {
-                acc[i][2 * q] = acc2[i][q].x;
-                acc[i][2 * q + 1] = acc2[i][q].y;
-            }
 #pragma unroll
         for (int i = 0; i < TW; ++i)
 #pragma unroll
@@ -602,34 +575,36 @@ cudaError_t launch_router_logits(const void* x, const float* w, float* logits, i
     return launch_tiled<64, 64, 8, 4>(xb, w, logits, tokens, h, experts, stream);
 }
 
-template <int EMAX, int TW, int JC, int STAGES, int WARPS = 8>
+template <int EMAX, int TW, int JC, int STAGES>
 static cudaError_t launch_staged(const void* x, const float* w, const float* bias, float* logits,
                                  int32_t* ids32, int64_t* ids64, float* weights, int64_t tokens,
                                  int64_t hidden, int experts, int topk, cudaStream_t stream) {
-    using R = StagedRouter<EMAX, TW, JC, STAGES, WARPS>;
+    using R = StagedRouter<EMAX, TW, JC, STAGES>;
     static int sms[64] = {};
     static bool configured[64] = {};
     int device = 0;
     MOE_CUDA_TRY(cudaGetDevice(&device));
     if (!configured[device & 63]) {
-        MOE_CUDA_TRY(cudaFuncSetAttribute(router_staged_kernel<EMAX, TW, JC, STAGES, WARPS>,
+        MOE_CUDA_TRY(cudaFuncSetAttribute(router_staged_kernel<EMAX, TW, JC, STAGES>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize, R::kSmemBytes));
         MOE_CUDA_TRY(cudaDeviceGetAttribute(&sms[device & 63], cudaDevAttrMultiProcessorCount, device));
         configured[device & 63] = true;
     }
     const int64_t sm = sms[device & 63];
     // Full blocks once there are at least as many as SMs; below that, fewer
-    // tokens per block (a multiple of TW) so that every SM gets one.
+    // tokens per block (a multiple of TW) so that every SM gets one.  At the
+    // Mixtral shape (4096 tokens) that is 147 blocks of 28 instead of 128 of
+    // 32: 20.9 against 22.8 us under ncu, equal (25.6 us) in an event loop.
+    // Eight experts' weights loaded together with j-outer packed FMAs, and 16
+    // warps of 2 tokens, were measured as well: no faster (26.6 and 31.7 us).
     int64_t block_tokens = R::kBlockTokens;
     if (tokens < sm * R::kBlockTokens) {
         block_tokens = ((tokens + sm - 1) / sm + TW - 1) / TW * TW;
         if (block_tokens < TW) block_tokens = TW;
     }
-    if (const char* env = getenv("MOE_B200_ROUTER_BLOCK_FULL"))  // tuning knob: full blocks
-        if (env[0] == '1') block_tokens = R::kBlockTokens;
     const int64_t blocks = (tokens + block_tokens - 1) / block_tokens;
     const unsigned grid = static_cast<unsigned>(blocks < sm ? blocks : sm);
-    router_staged_kernel<EMAX, TW, JC, STAGES, WARPS><<<grid, R::kThreads, R::kSmemBytes, stream>>>(
+    router_staged_kernel<EMAX, TW, JC, STAGES><<<grid, R::kThreads, R::kSmemBytes, stream>>>(
         static_cast<const __nv_bfloat16*>(x), w, bias, logits, ids32, ids64, weights, tokens,
         static_cast<int>(hidden), experts, topk, static_cast<int>(block_tokens));
     return cudaGetLastError();
@@ -641,13 +616,8 @@ cudaError_t launch_route(const void* x, const float* w, const float* bias, float
     if (tokens == 0) return cudaSuccess;
     // Measured on B200 (Mixtral router, T=4096, H=4096, E=8): 1024-element
     // chunks in two stages 25.6 us; 512 in four 31.7 us; 256 in six 48.0 us.
-    if (experts <= 8) {
-        // tuning knob: 16 compute warps of 2 tokens instead of 8 of 4 (same bits)
-        const char* env = getenv("MOE_B200_ROUTER_WARPS");
-        if (env && atoi(env) == 16)
-            return launch_staged<8, 2, 4, 2, 16>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
+    if (experts <= 8)
         return launch_staged<8, 4, 4, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
-    }
     if (experts <= 16)
         return launch_staged<16, 2, 4, 2>(x, w, bias, logits, ids32, ids64, weights, tokens, hidden, experts, topk, stream);
     if (experts <= kRouterSlicedMaxExperts)

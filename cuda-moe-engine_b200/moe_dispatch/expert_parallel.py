@@ -28,11 +28,11 @@ Two exchange backends:
   region of its HBM with the others through CUDA IPC.  Counts go out with peer
   stores and flags, senders write rows straight into the owners' expert-major
   buffers and owners write results straight back into the sources' packed
-  slots (``moe_ep_p2p``).  The exchange runs beside the gate/up GEMM, which
-  takes each expert's tiles in the order their rows arrive
-  (``moe_ep_p2p_gate_up``), and the down GEMM returns the rows itself
-  (``moe_ep_p2p_down_return``).  No host synchronisation: the whole step can
-  be captured in a CUDA graph.  Waits on peers are bounded and report through
+  slots (``moe_ep_p2p``); the down GEMM returns the rows itself
+  (``moe_ep_p2p_down_return``).  Optionally the exchange runs beside the
+  gate/up GEMM, which then takes each expert's tiles in the order their rows
+  arrive (``moe_ep_p2p_gate_up``, ``overlap=True``).  No host
+  synchronisation: the whole step can be captured in a CUDA graph.  Waits on peers are bounded and report through
   ``moe_device_status``.
 * ``"nccl"``: steps 3-4 and 8 as ``all_to_all_single`` with the split sizes
   read on the host (one synchronisation per forward), and the regroup kernels.
@@ -193,13 +193,17 @@ class ExpertParallelMoEBlock(torch.nn.Module):
     0.40 ms at the E=256 configuration and from 0.157 to 0.080 ms at the
     Mixtral shape, the down GEMM slows by 0.14 and 0.015 ms.
 
-    overlap=True (p2p with micro_batches=1, the default there) overlaps the row
-    exchange with the gate/up GEMM: this rank's own rows are copied first, the
-    other ranks' rows go out on a second stream, and the GEMM
-    (moe_ep_p2p_gate_up) takes each expert's tiles in the order their rows
-    arrive, waiting on a peer's rows flag before a tile that needs them.
-    Inside an expert the grouped rows follow that arrival order; GEMM rows are
-    independent, so the output bits do not change.
+    overlap=True (p2p with micro_batches=1) overlaps the row exchange with the
+    gate/up GEMM: this rank's own rows are copied first, the other ranks' rows
+    go out on a second stream, and the GEMM (moe_ep_p2p_gate_up) takes each
+    expert's tiles in the order their rows arrive, waiting on a peer's rows
+    flag before a tile that needs them.  Inside an expert the grouped rows
+    follow that arrival order; GEMM rows are independent, so the output bits
+    do not change.  It is off by default: on two B200s it measured slower
+    than the serial exchange (Mixtral shape 2.26-2.28 against 2.21 ms per
+    step, E=256 13.96-19.46 against 13.87 ms).  Tiles taken group by group
+    stream each expert's weights once per group, the send kernel beside the
+    GEMM slows it, and on fewer SMs the send itself slows (85-330 GB/s).
 
     micro_batches=m (p2p only) splits the local tokens into m consecutive
     slices, each with its own exchange region, run on their own streams in a
@@ -253,7 +257,7 @@ class ExpertParallelMoEBlock(torch.nn.Module):
         if self.micro_batches < 1 or (self.micro_batches > 1 and backend != "p2p"):
             raise ValueError("micro_batches must be 1, or >= 1 with the p2p backend")
         if overlap is None:
-            overlap = backend == "p2p" and self.micro_batches == 1
+            overlap = False
         if overlap and (backend != "p2p" or self.micro_batches != 1):
             raise ValueError("overlap needs the p2p backend and micro_batches=1")
         self.overlap = bool(overlap)
