@@ -362,51 +362,6 @@ def step_instrumented(block, x, events):
 STAGES = ("route", "dispatch", "gemm1", "gemm2", "combine")
 
 
-def graph_transport_times(block, x, repeats=10):
-    """Device time of the block's own dispatch and combine (its buffers, its
-    routing), each after a 256 MB L2 flush, timed by events recorded inside a
-    captured CUDA graph (external event nodes right around the stage): the
-    stage's kernels replay as one graph, with their programmatic launch
-    overlap and without the host-side launch latency that eager per-stage
-    events include.  Median over `repeats` replays.  Returns (dispatch ms,
-    combine ms)."""
-    state = block.workspace(x)
-    t = state.transport
-    out = {}
-    with torch.inference_mode():
-        ids32, ids64, weights = block.route(x)
-        flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=x.device)
-        bodies = {
-            "dispatch": lambda: t.dispatch(x, ids32, ids64),
-            "combine": lambda: t.combine(state.expert_output, weights),
-        }
-        stream = torch.cuda.Stream(device=x.device)
-        stream.wait_stream(torch.cuda.current_stream(x.device))
-        for name, body in bodies.items():
-            with torch.cuda.stream(stream):
-                for _ in range(2):  # warm
-                    flush.zero_()
-                    body()
-            torch.cuda.current_stream(x.device).wait_stream(stream)
-            start = torch.cuda.Event(enable_timing=True, external=True)
-            end = torch.cuda.Event(enable_timing=True, external=True)
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                flush.zero_()
-                start.record()
-                body()
-                end.record()
-            samples = []
-            for _ in range(repeats):
-                graph.replay()
-                torch.cuda.synchronize()
-                samples.append(start.elapsed_time(end))
-            out[name] = statistics.median(samples)
-            del graph
-        del flush
-    return out["dispatch"], out["combine"]
-
-
 def time_graph(block, x, steps, warmup, world, device, clocks_index=None):
     """K replays of a CUDA graph of one forward after W eager and 3+ graph
     warm-up steps; barrier + synchronize on both sides, max over ranks.
@@ -648,21 +603,6 @@ def run_ours(args, rank, world, local):
 
     rows = block.workspace(x).transport.packed.shape[0]
     summary = stage_summary(workload, tokens, stage, block, rows, tf_peak, hbm_peak)
-    try:
-        g_dispatch, g_combine = graph_transport_times(block, x)
-    except RuntimeError as err:  # events in a captured graph not supported: leave it out
-        g_dispatch = g_combine = None
-        summary["dispatch_combine_graph"] = {"unavailable": str(err).splitlines()[0]}
-    a_t = algorithmic(workload, tokens)
-    if g_dispatch is not None:
-        dc_graph = (a_t.dispatch + a_t.combine) / ((g_dispatch + g_combine) / 1e3) / 1e9
-        summary["dispatch_combine_graph"] = {
-            "what": "this block's dispatch and combine, each after a 256 MB L2 flush, timed by "
-                    "events recorded inside a captured CUDA graph around the stage (median of "
-                    "10 replays); dispatch_combine_frac_of_hbm above uses eager per-stage events",
-            "dispatch_ms": round(g_dispatch, 4), "combine_ms": round(g_combine, 4),
-            "gbs": round(dc_graph, 1), "frac_of_hbm": round(dc_graph / hbm_peak, 4),
-        }
     a = algorithmic(workload, tokens)
     gemm1_kernel, tile = gemm_kernel_name(block, rows, workload.experts)
     achieved = a.gemm1_flops / (stage["gemm1"] / 1e3) / 1e12
