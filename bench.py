@@ -44,7 +44,10 @@ With N > 1 (torchrun, one process per GPU) the block runs expert-parallel:
 the E experts are sharded evenly over the N ranks (rank r owns E/N of them),
 each rank routes its own T tokens (weak scaling), and token rows travel to
 their experts' ranks and back over NVLink peer memory (ExpertParallelMoEBlock,
-backend "p2p": no host sync, so the step is replayed as a CUDA graph;
+backend "p2p": no host sync, so the step is replayed as a CUDA graph; the
+down GEMM's epilogue stores the result rows straight back to their ranks
+(`--ep-fused-return 0` uses a separate return copy instead);
+`--ep-overlap 1` sends the rows beside an arrival-ordered gate/up GEMM;
 `--ep-backend nccl` uses NCCL all-to-all instead, eager, one host sync per step;
 `--ep-micro-batches m` pipelines m token slices so the exchanges overlap the
 previous slice's GEMMs).  Before timing, every rank runs the same tokens
