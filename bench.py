@@ -426,11 +426,12 @@ def time_stages(block, x, steps, world, device):
 def time_host_pipeline(block, x, steps, world, device):
     """Per-step ms of K batches through HostPipeline (pinned host in and out,
     per-slot CUDA graphs)."""
-    from moe_dispatch.host_pipeline import HostPipeline
+    from moe_dispatch.host_pipeline import HostPipeline, pinned_on_device_node
 
     pipe = HostPipeline(block, x.shape[0], device=device, graphs=True)
-    hosts = [x.cpu().pin_memory(), (x.cpu() * -1).pin_memory()]
-    outs = [torch.empty_like(hosts[0]).pin_memory() for _ in hosts]
+    # batches pinned on the GPU's own memory node (matters with several ranks per host)
+    hosts = pinned_on_device_node([x.cpu(), x.cpu() * -1], device)
+    outs = pinned_on_device_node([torch.empty_like(hosts[0]) for _ in hosts], device)
     pipe.run(hosts, outs)  # warm-up: fills both slots once
     stream = torch.cuda.current_stream(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

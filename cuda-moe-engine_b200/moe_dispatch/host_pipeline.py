@@ -19,11 +19,55 @@ Dependencies, per slot s (events on the device, no host synchronisation):
     load(i)    waits computed[s] of batch i-slots (x[s] free), records loaded[s]
     compute(i) waits loaded[s] and stored[s] (y[s] free), records computed[s]
     store(i)   waits computed[s], records stored[s]
+
+With one process per GPU on a multi-socket host, allocate each process's
+pinned batches on the memory node of its GPU: `device_local_cpus(device)`
+gives that GPU's local CPU set (from NVML), and pinned memory allocated while
+the process runs on those CPUs is placed on their node.
 """
 
 from __future__ import annotations
 
+import os
+
 import torch
+
+
+def device_local_cpus(device):
+    """The CPU cores attached to `device`'s socket, as a set (NVML's CPU
+    affinity of the GPU, matched by PCI bus id), or None when NVML or the
+    GPU's PCI location is not available.  Reads only; changes nothing."""
+    try:
+        import pynvml
+
+        props = torch.cuda.get_device_properties(torch.device(device))
+        bus_id = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus_id)
+            words = (os.cpu_count() + 63) // 64
+            mask = pynvml.nvmlDeviceGetCpuAffinity(handle, words)
+        finally:
+            pynvml.nvmlShutdown()
+    except Exception:  # no NVML, no GPU, or a driver that does not report it
+        return None
+    cpus = {64 * w + b for w, bits in enumerate(mask) for b in range(64) if (int(bits) >> b) & 1}
+    return cpus or None
+
+
+def pinned_on_device_node(tensors, device):
+    """Pinned copies of host `tensors`, allocated while this process runs on
+    the CPUs local to `device` (so their pages land on that GPU's memory
+    node); the process's CPU affinity is restored afterwards."""
+    cpus = device_local_cpus(device)
+    previous = os.sched_getaffinity(0) if hasattr(os, "sched_getaffinity") else None
+    if cpus and previous is not None and cpus & previous:
+        os.sched_setaffinity(0, cpus & previous)
+    try:
+        return [t.contiguous().pin_memory() for t in tensors]
+    finally:
+        if cpus and previous is not None:
+            os.sched_setaffinity(0, previous)
 
 
 class HostPipeline:
