@@ -59,6 +59,10 @@ struct TiledRouter {
     static_assert(MT % 4 == 0 && ME % 4 == 0, "float4 micro-tile loads");
 };
 
+// Inside a full chunk the next k-step's shared-memory operands are loaded
+// before the current step's FMAs (two register sets), so the loads' latency
+// hides behind the packed FMAs: 2-4 % faster than the plain loop at E = 64 and
+// E = 256 (the kernel is latency-bound), same values.
 template <int TT, int TE, int MT, int ME>
 __global__ void __launch_bounds__(TiledRouter<TT, TE, MT, ME>::kThreads, 2)
 router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
@@ -134,9 +138,7 @@ router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
 #pragma unroll
         for (int j = 0; j < NH; ++j) acc[i][j] = make_float2(0.0f, 0.0f);
 
-    auto step = [&](const float* xk, const float* wk) {
-        float xv[MT];
-        float2 wv[NH];
+    auto operands = [&](const float* xk, const float* wk, float (&xv)[MT], float2 (&wv)[NH]) {
         const float4 x0 = *reinterpret_cast<const float4*>(xk + ty * MH);
         const float4 x1 = *reinterpret_cast<const float4*>(xk + TT / 2 + ty * MH);
         xv[0] = x0.x; xv[1] = x0.y; xv[2] = x0.z; xv[3] = x0.w;
@@ -150,12 +152,20 @@ router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
             wv[0] = *reinterpret_cast<const float2*>(wk + tx * NH);
             wv[1] = *reinterpret_cast<const float2*>(wk + TE / 2 + tx * NH);
         }
+    };
+    auto fmas = [&](const float (&xv)[MT], const float2 (&wv)[NH]) {
 #pragma unroll
         for (int i = 0; i < MT; ++i) {
             const float2 xx = make_float2(xv[i], xv[i]);
 #pragma unroll
             for (int j = 0; j < NH; ++j) acc[i][j] = __ffma2_rn(xx, wv[j], acc[i][j]);
         }
+    };
+    auto step = [&](const float* xk, const float* wk) {
+        float xv[MT];
+        float2 wv[NH];
+        operands(xk, wk, xv, wv);
+        fmas(xv, wv);
     };
 
     load(0);
@@ -168,8 +178,16 @@ router_logits_tiled_kernel(const __nv_bfloat16* __restrict__ x, const float* __r
         const float* wb = ws + buf * KC * TE;
         const int steps = min(KC, hidden - h0);
         if (steps == KC) {
-#pragma unroll 8
-            for (int k = 0; k < KC; ++k) step(xb + k * TT, wb + k * TE);
+            float xa[MT], xn[MT];
+            float2 wa[NH], wn[NH];
+            operands(xb, wb, xa, wa);
+#pragma unroll
+            for (int k = 0; k < KC; k += 2) {
+                operands(xb + (k + 1) * TT, wb + (k + 1) * TE, xn, wn);
+                fmas(xa, wa);
+                if (k + 2 < KC) operands(xb + (k + 2) * TT, wb + (k + 2) * TE, xa, wa);
+                fmas(xn, wn);
+            }
         } else {
             for (int k = 0; k < steps; ++k) step(xb + k * TT, wb + k * TE);
         }
@@ -563,9 +581,11 @@ cudaError_t launch_router_logits(const void* x, const float* w, float* logits, i
     const auto* xb = static_cast<const __nv_bfloat16*>(x);
     const int h = static_cast<int>(hidden);
     // Tile (tokens x experts) per CTA; MOE_B200_ROUTER_TILE overrides the
-    // choice (a tuning knob: every tile gives the same bits).  Measured on B200:
-    // E=256, H=7168, T=32768: 64x128 2.88 ms, 128x128 3.14, 128x64 3.31, 64x64
-    // 3.59; E=64, H=2048, T=16384: 128x64 0.187 ms, 64x64 0.198, 32x64 0.229.
+    // choice (a tuning knob: every tile gives the same bits).  Measured on B200
+    // (L2 flushed before each launch), E=256, H=7168: 64x128 is the fastest at
+    // 4096, 8192 and 32768 tokens (0.46, 0.83, 2.84 ms; 128x128 0.92, 0.93,
+    // 3.13; 128x64 0.51, 0.98, 3.30; 64x64 0.55, 1.05, 3.56; 32x64 0.66, 1.28,
+    // 4.33); E=64, H=2048, T=16384: 128x64 0.159 ms, 64x64 0.175, 32x64 0.204.
     const char* env = getenv("MOE_B200_ROUTER_TILE");
     const char* pick = env ? env : (experts <= 64 ? "128x64" : "64x128");
     if (strcmp(pick, "128x128") == 0) return launch_tiled<128, 128, 8, 8>(xb, w, logits, tokens, h, experts, stream);
