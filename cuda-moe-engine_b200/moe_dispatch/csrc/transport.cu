@@ -39,16 +39,19 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
                       int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
                       int32_t* __restrict__ slots, int32_t* __restrict__ scratch) {
     extern __shared__ int32_t smem[];
-    int32_t* hist = smem;                     // [32][E] per-warp counts of this round
-    int32_t* base = smem + 32 * experts;      // [32][E] per-warp bases of this round
-    int32_t* running = smem + 64 * experts;   // [E] chunk-local running totals
+    // rows of E + 1 words: lane w of a warp scanning expert x reads word
+    // w * (E + 1) + x, on 32 different banks whatever E is
+    const int stride = experts + 1;
+    int32_t* hist = smem;                     // [32][E+1] per-warp counts of this round
+    int32_t* base = smem + 32 * stride;       // [32][E+1] per-warp bases of this round
+    int32_t* running = smem + 64 * stride;    // [E] chunk-local running totals
     __shared__ int is_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The pack kernel may start now: it reads its token rows, then waits for
     // this grid (griddepcontrol.wait) before it needs anything computed here.
     pdl_trigger();
-    for (int i = tid; i < 32 * experts; i += kIndexThreads) hist[i] = 0;
+    for (int i = tid; i < 32 * stride; i += kIndexThreads) hist[i] = 0;
     for (int i = tid; i < experts; i += kIndexThreads) running[i] = 0;
     pdl_wait();  // the ids come from the kernel before (the router)
     __syncthreads();
@@ -62,20 +65,26 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
         const unsigned key = valid ? static_cast<unsigned>(e) : static_cast<unsigned>(experts + lane);
         const unsigned peers = __match_any_sync(0xffffffffu, key);
         const int rank = __popc(peers & lanes_below);
-        if (valid && rank == 0) hist[warp * experts + e] = __popc(peers);
+        if (valid && rank == 0) hist[warp * stride + e] = __popc(peers);
         __syncthreads();
-        for (int x = tid; x < experts; x += kIndexThreads) {
-            int run = running[x];
-            for (int w = 0; w < 32; ++w) {
-                const int c = hist[w * experts + x];
-                base[w * experts + x] = run;
-                hist[w * experts + x] = 0;
-                run += c;
+        // each expert's 32 per-warp counts, scanned in warp order by one warp
+        // (lane = warp index): exclusive prefix + running total = its base
+        for (int x = warp; x < experts; x += kIndexThreads / 32) {
+            const int c = hist[lane * stride + x];
+            int inclusive = c;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, inclusive, off);
+                if (lane >= off) inclusive += y;
             }
-            running[x] = run;
+            const int run = running[x];
+            base[lane * stride + x] = run + inclusive - c;
+            hist[lane * stride + x] = 0;
+            __syncwarp();
+            if (lane == 31) running[x] = run + inclusive;
         }
         __syncthreads();
-        if (p < n) slots[p] = valid ? base[warp * experts + e] + rank : -1;
+        if (p < n) slots[p] = valid ? base[warp * stride + e] + rank : -1;
         const unsigned bad = __ballot_sync(0xffffffffu, p < n && !valid);
         if (bad && lane == 0) atomicAdd(scratch + 1, __popc(bad));
     }
@@ -503,14 +512,14 @@ cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_
                             cudaStream_t stream) {
     const int64_t n = tokens * topk;
     const int64_t chunks = n > 0 ? (n + kDispatchChunk - 1) / kDispatchChunk : 1;
-    const size_t smem = static_cast<size_t>(65 * experts) * sizeof(int32_t);
+    const size_t smem = static_cast<size_t>(65 * experts + 64) * sizeof(int32_t);
     static bool configured[64] = {};
     int device = 0;
     MOE_CUDA_TRY(cudaGetDevice(&device));
     if (!configured[device & 63]) {  // once per device, for the largest expert count
         MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          65 * kMaxDispatchExperts * static_cast<int>(sizeof(int32_t))));
+                                          (65 * kMaxDispatchExperts + 64) * static_cast<int>(sizeof(int32_t))));
         configured[device & 63] = true;
     }
     MOE_CUDA_TRY(launch_dependent(dispatch_index_kernel, dim3(static_cast<unsigned>(chunks)),
