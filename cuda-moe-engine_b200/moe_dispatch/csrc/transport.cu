@@ -11,7 +11,9 @@
 //                          its rank inside the chunk without atomics.  The last
 //                          CTA to finish (ticket in scratch) scans the per-chunk
 //                          counts into chunk bases, writes counts[E] and the
-//                          padded offsets[E+1].
+//                          padded offsets[E+1].  Up to 8 chunks the CTAs form
+//                          one cluster and hand their counts to CTA 0 through
+//                          distributed shared memory instead.
 //   pack_kernel            one CTA per token: reads the x row once, writes it to
 //                          its K packed rows (16-byte vectors), writes slots and
 //                          inverse; E extra CTAs zero the padding rows.
@@ -34,10 +36,21 @@ template <> struct VecOf<8> { using T = uint2; };
 template <> struct VecOf<4> { using T = uint32_t; };
 template <> struct VecOf<2> { using T = uint16_t; };
 
+// Up to this many chunks the index CTAs run as one thread-block cluster: the
+// chunk totals travel to the leader CTA through distributed shared memory and
+// a cluster barrier, instead of through the global chunk table, a fence, the
+// completion ticket and the last CTA's reads (Mixtral shape: 8 chunks).
+constexpr int kClusterChunks = 8;
+
+__device__ __forceinline__ uint32_t shared_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+template <bool kCluster>
 __global__ void __launch_bounds__(kIndexThreads)
 dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, int alignment,
                       int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
-                      int32_t* __restrict__ slots, int32_t* __restrict__ scratch) {
+                      int32_t* __restrict__ slots, int32_t* __restrict__ scratch, int chunks) {
     extern __shared__ int32_t smem[];
     // rows of E + 1 words: lane w of a warp scanning expert x reads word
     // w * (E + 1) + x, on 32 different banks whatever E is
@@ -45,7 +58,12 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
     int32_t* hist = smem;                     // [32][E+1] per-warp counts of this round
     int32_t* base = smem + 32 * stride;       // [32][E+1] per-warp bases of this round
     int32_t* running = smem + 64 * stride;    // [E] chunk-local running totals
+    // cluster form: [kClusterChunks][E] chunk totals and [kClusterChunks]
+    // out-of-range counts, filled in the leader CTA by every CTA of the cluster
+    int32_t* table = running + experts;
+    int32_t* bad_slots = table + kClusterChunks * experts;
     __shared__ int is_last;
+    __shared__ int bad_here;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     // The pack kernel may start now: it reads its token rows, then waits for
@@ -53,6 +71,10 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
     pdl_trigger();
     for (int i = tid; i < 32 * stride; i += kIndexThreads) hist[i] = 0;
     for (int i = tid; i < experts; i += kIndexThreads) running[i] = 0;
+    if (tid == 0) bad_here = 0;
+    // cluster form: announce this CTA has started; its peers wait for that
+    // before they store into the leader's shared memory
+    if constexpr (kCluster) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     pdl_wait();  // the ids come from the kernel before (the router)
     __syncthreads();
 
@@ -86,11 +108,47 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
         __syncthreads();
         if (p < n) slots[p] = valid ? base[warp * stride + e] + rank : -1;
         const unsigned bad = __ballot_sync(0xffffffffu, p < n && !valid);
-        if (bad && lane == 0) atomicAdd(scratch + 1, __popc(bad));
+        if (bad && lane == 0) {
+            if constexpr (kCluster) atomicAdd(&bad_here, __popc(bad));
+            else atomicAdd(scratch + 1, __popc(bad));
+        }
     }
 
     int32_t* ticket = scratch;
     int32_t* chunk_table = scratch + kScratchHeader;  // [chunks][E]
+    if constexpr (kCluster) {
+        // this CTA's chunk totals (and bad-id count) into the leader's table
+        __syncthreads();
+        asm volatile("barrier.cluster.wait.aligned;" ::: "memory");  // every CTA has started
+        const uint32_t me = blockIdx.x;  // the grid is one cluster
+        for (int x = tid; x < experts; x += kIndexThreads) {
+            uint32_t remote;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                         : "=r"(remote) : "r"(shared_u32(table + me * experts + x)));
+            asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(remote), "r"(running[x]) : "memory");
+        }
+        if (tid == 0) {
+            uint32_t remote;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, 0;"
+                         : "=r"(remote) : "r"(shared_u32(bad_slots + me)));
+            asm volatile("st.shared::cluster.s32 [%0], %1;" ::"r"(remote), "r"(bad_here) : "memory");
+        }
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                     ::: "memory");
+        if (me != 0) return;
+        // leader: chunk bases (exclusive over the chunks, in chunk order),
+        // counts and the aligned totals the offsets scan below uses
+        for (int x = tid; x < experts; x += kIndexThreads) {
+            int carry = 0;
+            for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+                const int v = table[c * experts + x];
+                if (c < chunks) chunk_table[static_cast<int64_t>(c) * experts + x] = carry;
+                carry += v;
+            }
+            counts[x] = carry;
+            running[x] = alignment > 1 ? (carry + alignment - 1) / alignment * alignment : carry;
+        }
+    } else {
     for (int x = tid; x < experts; x += kIndexThreads)
         chunk_table[static_cast<int64_t>(blockIdx.x) * experts + x] = running[x];
     __threadfence();
@@ -137,6 +195,7 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
             }
         }
     }
+    }  // kCluster
     __syncthreads();
     if (warp == 0) {
         const int per = (experts + 31) / 32;
@@ -156,8 +215,14 @@ dispatch_index_kernel(const int32_t* __restrict__ ids, int64_t n, int experts, i
         }
         if (lane == 31) offsets[experts] = inclusive;
         if (lane == 0) {
-            scratch[2] = atomicExch(scratch + 1, 0);  // out-of-range ids of this call
-            *ticket = 0;  // ready for the next call
+            if constexpr (kCluster) {
+                int bad_total = 0;
+                for (int c = 0; c < static_cast<int>(gridDim.x); ++c) bad_total += bad_slots[c];
+                scratch[2] = bad_total;  // out-of-range ids of this call
+            } else {
+                scratch[2] = atomicExch(scratch + 1, 0);  // out-of-range ids of this call
+                *ticket = 0;  // ready for the next call
+            }
         }
     }
 }
@@ -512,19 +577,49 @@ cudaError_t launch_dispatch(const void* x, int dtype, const int32_t* ids, int32_
                             cudaStream_t stream) {
     const int64_t n = tokens * topk;
     const int64_t chunks = n > 0 ? (n + kDispatchChunk - 1) / kDispatchChunk : 1;
+    // [32][E+1] x 2 + [E], and for the cluster form [8][E] + [8]
     const size_t smem = static_cast<size_t>(65 * experts + 64) * sizeof(int32_t);
+    const size_t cluster_smem = smem + static_cast<size_t>(kClusterChunks * (experts + 1)) * sizeof(int32_t);
     static bool configured[64] = {};
     int device = 0;
     MOE_CUDA_TRY(cudaGetDevice(&device));
     if (!configured[device & 63]) {  // once per device, for the largest expert count
-        MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel,
+        MOE_CUDA_TRY(cudaFuncSetAttribute(dispatch_index_kernel<false>,
                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (65 * kMaxDispatchExperts + 64) * static_cast<int>(sizeof(int32_t))));
+        MOE_CUDA_TRY(cudaFuncSetAttribute(
+            dispatch_index_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            (65 * kMaxDispatchExperts + 64 + kClusterChunks * (kMaxDispatchExperts + 1)) *
+                static_cast<int>(sizeof(int32_t))));
         configured[device & 63] = true;
     }
-    MOE_CUDA_TRY(launch_dependent(dispatch_index_kernel, dim3(static_cast<unsigned>(chunks)),
-                                  dim3(kIndexThreads), smem, stream, ids, n, experts, alignment,
-                                  counts, offsets, slots, scratch));
+    const char* cluster_env = getenv("MOE_B200_INDEX_CLUSTER");  // tuning knob: 0 = never
+    if (chunks <= kClusterChunks && !(cluster_env && cluster_env[0] == '0')) {
+        // one cluster of the next power of two CTAs; those past `chunks` see no ids
+        unsigned size = 1;
+        while (size < chunks) size <<= 1;
+        cudaLaunchConfig_t config = {};
+        cudaLaunchAttribute attribute[2];
+        attribute[0].id = cudaLaunchAttributeClusterDimension;
+        attribute[0].val.clusterDim.x = size;
+        attribute[0].val.clusterDim.y = 1;
+        attribute[0].val.clusterDim.z = 1;
+        attribute[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attribute[1].val.programmaticStreamSerializationAllowed = 1;
+        config.gridDim = dim3(size);
+        config.blockDim = dim3(kIndexThreads);
+        config.dynamicSmemBytes = cluster_smem;
+        config.stream = stream;
+        config.attrs = attribute;
+        config.numAttrs = 2;
+        MOE_CUDA_TRY(cudaLaunchKernelEx(&config, dispatch_index_kernel<true>, ids, n, experts,
+                                        alignment, counts, offsets, slots, scratch,
+                                        static_cast<int>(chunks)));
+    } else {
+        MOE_CUDA_TRY(launch_dependent(dispatch_index_kernel<false>, dim3(static_cast<unsigned>(chunks)),
+                                      dim3(kIndexThreads), smem, stream, ids, n, experts, alignment,
+                                      counts, offsets, slots, scratch, static_cast<int>(chunks)));
+    }
     const int32_t* table = scratch + kScratchHeader;
     const int64_t row_bytes = hidden * dtype_bytes(dtype);
     switch (vector_bytes) {
