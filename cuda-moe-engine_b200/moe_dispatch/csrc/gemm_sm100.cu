@@ -1184,6 +1184,354 @@ grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
     }
 }
 
+// ------------------------------------------------------ operand-swapped pair tile
+//
+// The pair tile pads each expert's rows up to a multiple of 256, the MMA's M.
+// Here the operands trade places: the weights are the M side (256 weight rows
+// per tile, 128 in each CTA) and an expert's packed rows are the N side, which
+// the instruction descriptor sets per tile in steps of 16.  An expert of R
+// rows runs mt = ceil(R / 256) tiles of N = round_up(ceil(R / mt), 16) rows,
+// so 1032 rows cost 5 x 208 MMA columns instead of 5 x 256 padded rows.  TMEM
+// then holds out^T (lane = output column, TMEM column = packed row); the
+// epilogue transposes each 32 x 32 chunk through shared memory and stores
+// 64-byte row segments.
+//
+// SwiGLU: each CTA's 128 weight rows are 64 gate rows (TMEM lanes 0..63) and
+// the matching 64 up rows (lanes 64..127).  A gate warp and the up warp of the
+// same lanes and column group swap halves of each 32 x 32 chunk through shared
+// memory (the gate warp gives its bf16-rounded g of rows 16..31, the up warp
+// its u of rows 0..15; two buffers per warp pair, an mbarrier handshake with
+// bounded waits), then each applies silu(g) * u to its 16 rows and stores
+// them, so all eight epilogue warps share the SwiGLU work.
+//
+// The fp32 accumulation is the same sum over k in the same order as the other
+// tiles, so the results are bit-identical to them (tested).
+constexpr int kSwapPairs = 4;  // SwiGLU warp pairs (gate warp + up warp)
+constexpr int kSwapBarrierBytes = (2 * kPairStages + 5 + 2 * kTileRing + 4 * kSwapPairs) * 8;
+constexpr int kSwapStageOffset = (kPairStages * kPairStageBytes + kSwapBarrierBytes + 16 +
+                                  kTileRing * 4 + kTableBytes + 127) / 128 * 128;
+constexpr int kSwapStageBytes = (kEpilogueThreads / 32) * 2048;  // a 32 x 32 bf16 chunk per warp
+constexpr int kSwapSmemBytes = 1024 + kSwapStageOffset + kSwapStageBytes;
+static_assert(kSwapSmemBytes <= 227 * 1024, "swapped pair tile fits in shared memory");
+
+// Packed rows in each of an expert's mt tiles (the MMA's N): the rows spread
+// evenly over the tiles, rounded up to the N step of 16.  Never above 256,
+// and the last tile always holds at least one real row.
+__device__ __forceinline__ int swap_tile_cols(int rows, int mt) {
+    return ((rows + mt - 1) / mt + 15) & ~15;
+}
+
+template <bool kSwiglu>
+__global__ void __launch_bounds__(kThreads, 1)
+grouped_gemm_swap_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                         const __grid_constant__ CUtensorMap tmap_b, const GemmParams p,
+                         const GemmScatter) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* tiles = smem;  // per stage: 128 weight rows, then 128 packed rows
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kPairStages * kPairStageBytes);
+    uint64_t* empty = full + kPairStages;
+    uint64_t* tmem_full = empty + kPairStages;
+    uint64_t* tmem_empty = tmem_full + 2;
+    uint64_t* drain = tmem_empty + 2;
+    uint64_t* tile_full = drain + 1;
+    uint64_t* tile_empty = tile_full + kTileRing;   // used in the leader only
+    uint64_t* x_ready = tile_empty + kTileRing;     // [pair][buffer] up values written
+    uint64_t* x_free = x_ready + 2 * kSwapPairs;    // [pair][buffer] buffer consumed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_free + 2 * kSwapPairs);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* tile_ring = reinterpret_cast<volatile int*>(tmem_slot + 4);
+    int* mt_prefix = reinterpret_cast<int*>(tmem_slot + 4 + kTileRing);
+    int* offs = mt_prefix + kMaxExperts + 1;
+    int* tbase = offs + kMaxExperts + 1;
+    __nv_bfloat16* chunks = reinterpret_cast<__nv_bfloat16*>(smem + kSwapStageOffset);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0 = leader, 1 = peer
+    const bool leader = rank == 0;
+    constexpr int kOutTile = kSwiglu ? kBN / 2 : kBN;  // output columns of a tile (both CTAs)
+    const int k_blocks = (p.k_dim + kBK - 1) / kBK;
+    if (threadIdx.x == 32) enter_schedule(p.sched);
+    pdl_trigger();  // the next kernel may launch and run its prologue
+
+    if (warp == 0) {
+        pdl_wait();  // offsets and rows come from the kernels before this launch
+        build_tile_table<kPairBM>(p, lane, mt_prefix, offs, tbase);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int s = 0; s < kPairStages; ++s) {
+                mbar_init(&full[s], 1);
+                mbar_init(&empty[s], 1);
+            }
+            for (int a = 0; a < 2; ++a) {
+                mbar_init(&tmem_full[a], 1);
+                mbar_init(&tmem_empty[a], 2 * kEpilogueThreads);
+            }
+            for (int r = 0; r < kTileRing; ++r) {
+                mbar_init(&tile_full[r], 1);
+                mbar_init(&tile_empty[r], 2 + 2 * kEpilogueThreads);
+            }
+            for (int i = 0; i < 2 * kSwapPairs; ++i) {  // both warps of a pair arrive
+                mbar_init(&x_ready[i], 64);
+                mbar_init(&x_free[i], 64);
+            }
+            mbar_init(drain, 1);
+            *abort_flag = 0;
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        }
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(tmem_slot)),
+                     "r"(kTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    }
+    if (warp != 0) pdl_wait();
+    tc_fence_before();
+    cluster_sync();  // barriers initialised and TMEM allocated in both CTAs
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int pairs = p.experts;  // one arrival group
+    const int total_tiles = mt_prefix[pairs] * p.n_tiles;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA producer (both CTAs)
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t armed = 0, last_parity = 0;
+            int ring = 0;
+            uint32_t ring_phase = 0;
+            int next = leader ? claim_tile(p.sched, total_tiles) : -1;
+            for (;;) {
+                int t;
+                if (leader) {
+                    t = *abort_flag ? -1 : next;
+                    if (!mbar_wait(&tile_empty[ring], ring_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                    tile_ring[ring] = t;
+                    st_cluster_s32(map_to_cta(smem_u32(const_cast<int*>(&tile_ring[ring])), 1), t);
+                    mbar_arrive(&tile_full[ring]);
+                    mbar_arrive_cluster(map_to_cta(smem_u32(&tile_full[ring]), 1));
+                } else {
+                    if (!mbar_wait_cluster(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+                    t = tile_ring[ring];
+                    mbar_arrive_cluster(map_to_cta(smem_u32(&tile_empty[ring]), 0));
+                }
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
+                if (leader) next = claim_tile(p.sched, total_tiles);
+                int j, m, n;
+                decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+                const int cols = swap_tile_cols(offs[j + 1] - offs[j], mt_prefix[j + 1] - mt_prefix[j]);
+                // this CTA's packed rows: the first or second half of the tile's N
+                const int row0 = tbase[j] + m * cols + static_cast<int>(rank) * (cols >> 1);
+                // this CTA's weight rows: 64 gate (+ 64 up) or 128 output columns
+                const int wrow = j * p.b_rows + n * kOutTile + static_cast<int>(rank) * (kOutTile / 2);
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t leader_full = map_to_cta(smem_u32(&full[stage]), 0);
+                    uint8_t* sw = tiles + stage * kPairStageBytes;
+                    if (leader) mbar_expect_tx(&full[stage], 2 * kPairStageBytes);
+                    if constexpr (kSwiglu) {
+                        // two 64-row boxes: gate rows, then the matching up rows
+                        tma_load_2d_pair(sw, &tmap_b, leader_full, kb * kBK, wrow);
+                        tma_load_2d_pair(sw + kPairTileABytes / 2, &tmap_b, leader_full, kb * kBK,
+                                         wrow + p.up_offset);
+                    } else {
+                        tma_load_2d_pair(sw, &tmap_b, leader_full, kb * kBK, wrow);
+                    }
+                    tma_load_2d_pair(sw + kPairTileABytes, &tmap_a, leader_full, kb * kBK, row0);
+                    armed |= 1u << stage;
+                    last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+            }
+            if (*abort_flag && leader) {
+                for (int s = 0; s < kPairStages; ++s)
+                    if (armed & (1u << s)) {
+                        volatile int never = 0;
+                        mbar_wait(&full[s], (last_parity >> s) & 1u, &never, kDrainLimitNs);
+                    }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && leader) {
+            // ------------------------------------------------ MMA issuer (leader only)
+            constexpr uint32_t idesc_m = make_idesc(kPairBM, 0);  // N is set per tile
+            int stage = 0;
+            uint32_t phase = 0;
+            int ring = 0;
+            uint32_t ring_phase = 0;
+            bool issued = false;
+            for (int local = 0;; ++local) {
+                if (!mbar_wait(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+                const int t = tile_ring[ring];
+                mbar_arrive(&tile_empty[ring]);
+                if (++ring == kTileRing) {
+                    ring = 0;
+                    ring_phase ^= 1u;
+                }
+                if (t < 0) break;
+                int j, m, n;
+                decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+                const int cols = swap_tile_cols(offs[j + 1] - offs[j], mt_prefix[j + 1] - mt_prefix[j]);
+                const uint32_t idesc = idesc_m | (static_cast<uint32_t>(cols >> 3) << 17);
+                const int acc = local & 1;
+                const uint32_t acc_phase = (local >> 1) & 1;
+                if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, abort_flag, kWaitLimitNs)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + acc * kBN;
+                bool ok = true;
+                for (int kb = 0; kb < k_blocks; ++kb) {
+                    if (!mbar_wait(&full[stage], phase, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t w_addr = smem_u32(tiles + stage * kPairStageBytes);
+                    const uint32_t r_addr = w_addr + kPairTileABytes;
+#pragma unroll
+                    for (int k = 0; k < kBK / kUmmaK; ++k)
+                        umma_bf16_pair(d, smem_desc_sw128(w_addr + k * kUmmaK * 2),
+                                       smem_desc_sw128(r_addr + k * kUmmaK * 2), idesc,
+                                       (kb | k) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit_pair(&empty[stage]);
+                    if (++stage == kPairStages) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                umma_commit_pair(&tmem_full[acc]);
+            }
+            if (*abort_flag && issued) {
+                umma_commit_pair(drain);
+                volatile int never = 0;
+                mbar_wait(drain, 0, &never, kDrainLimitNs);
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue (both CTAs)
+        const int quarter = warp & 3;
+        const int group = (warp - 2) >> 2;  // even or odd 32-column chunks of the tile
+        const bool up_warp = kSwiglu && quarter >= 2;
+        const int xpair = (quarter & 1) + 2 * group;  // SwiGLU: gate warp + up warp
+        __nv_bfloat16* mine = chunks + (kSwiglu ? 2 * xpair : warp - 2) * 1024;
+        // first output column of this warp's 32 TMEM lanes
+        const int lane_col = static_cast<int>(rank) * (kOutTile / 2) + (kSwiglu ? (quarter & 1) : quarter) * 32;
+        const uint32_t leader_empty0 = map_to_cta(smem_u32(&tmem_empty[0]), 0);
+        const uint32_t leader_empty1 = map_to_cta(smem_u32(&tmem_empty[1]), 0);
+        uint32_t handed = 0;  // chunks passed between the SwiGLU warp pair so far
+        int ring = 0;
+        uint32_t ring_phase = 0;
+        bool ok = true;
+        for (int local = 0; ok; ++local) {
+            if (!mbar_wait_cluster(&tile_full[ring], ring_phase, abort_flag, kWaitLimitNs)) break;
+            const int t = tile_ring[ring];
+            mbar_arrive_cluster(map_to_cta(smem_u32(&tile_empty[ring]), 0));
+            if (++ring == kTileRing) {
+                ring = 0;
+                ring_phase ^= 1u;
+            }
+            if (t < 0) break;
+            int j, m, n;
+            decode_tile(t, mt_prefix, pairs, p.n_tiles, j, m, n);
+            const int cols = swap_tile_cols(offs[j + 1] - offs[j], mt_prefix[j + 1] - mt_prefix[j]);
+            const int first = tbase[j] + m * cols;           // packed row of TMEM column 0
+            const int real = min(cols, offs[j + 1] - first);  // columns holding real rows
+            const int acc = local & 1;
+            const uint32_t acc_phase = (local >> 1) & 1;
+            if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, kWaitLimitNs)) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * kBN;
+            const int col0 = n * kOutTile + lane_col;
+#pragma unroll 1
+            for (int c = group * 32; c < real; c += 64) {
+                uint32_t v[32];
+                tmem_ld32(taddr + c, v);
+                tmem_wait_ld();
+                // chunk[i][l]: packed row c + i, output column col0 + l
+                __nv_bfloat16* chunk = mine;
+                int buffer = 0;
+                int first_row = 0, steps = 4;  // rows of the chunk this warp stores
+                if constexpr (kSwiglu) {
+                    buffer = 2 * xpair + (handed & 1);
+                    const uint32_t use = (handed >> 1) & 1;
+                    ++handed;
+                    chunk = chunks + buffer * 1024;
+                    // the gate warp keeps rows 0..15, the up warp rows 16..31
+                    first_row = up_warp ? 16 : 0;
+                    steps = 2;
+                    const int give = 16 - first_row;
+                    if (!mbar_wait(&x_free[buffer], use ^ 1u, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)  // constant register indices, a warp-uniform select
+                        chunk[(give + i) * 32 + lane] =
+                            __float2bfloat16_rn(__uint_as_float(up_warp ? v[i] : v[16 + i]));
+                    mbar_arrive(&x_ready[buffer]);
+                    if (!mbar_wait(&x_ready[buffer], use, abort_flag, kWaitLimitNs)) {
+                        ok = false;
+                        break;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int row = first_row + i;
+                        const float mine_v = round_bf16(__uint_as_float(up_warp ? v[16 + i] : v[i]));
+                        const float other = __bfloat162float(chunk[row * 32 + lane]);
+                        const float g = up_warp ? other : mine_v;
+                        const float up = up_warp ? mine_v : other;
+                        chunk[row * 32 + lane] = __float2bfloat16_rn((g / (1.0f + expf(-g))) * up);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        chunk[i * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[i]));
+                }
+                __syncwarp();
+                // packed row r of the chunk: 32 outputs, four 16-byte pieces;
+                // lanes 4r..4r+3 store row r, eight rows per instruction
+                const uint4* pieces = reinterpret_cast<const uint4*>(chunk);
+#pragma unroll
+                for (int step = 0; step < steps; ++step) {
+                    const int r = first_row + step * 8 + (lane >> 2), q = lane & 3;
+                    const int col = col0 + q * 8;
+                    if (c + r < real && col + 8 <= p.n_out)
+                        *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(first + c + r) * p.ldo + col) =
+                            pieces[r * 4 + q];
+                }
+                __syncwarp();
+                if constexpr (kSwiglu) mbar_arrive(&x_free[buffer]);
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(acc ? leader_empty1 : leader_empty0);
+        }
+    }
+
+    tc_fence_before();
+    cluster_sync();  // no CTA leaves while its peer may still touch its memory
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                     "r"(kTmemCols));
+    }
+    if (threadIdx.x == 0) finish_schedule(p.sched);
+}
+
 // ------------------------------------------------------------------ host side
 
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
@@ -1224,6 +1572,8 @@ struct DeviceInfo {
     uint32_t* sched = nullptr;  // device address of g_tile_sched
     bool configured[2][2] = {};       // [fp8][swiglu]
     bool pair_configured[2][2] = {};  // [fp8][swiglu]
+    bool swap_configured[2] = {};     // [swiglu]
+    int swap_clusters = 0;
 };
 
 DeviceInfo& device_info(int device) {
@@ -1265,6 +1615,13 @@ Tile pick_tile(int64_t rows, int experts) {
     if (env && strcmp(env, "pair") == 0) return Tile::kPair;
     if (env && strcmp(env, "single") == 0) return Tile::kSingle;
     return rows >= 512 * static_cast<int64_t>(experts) ? Tile::kPair : Tile::kSingle;
+}
+
+// The operand-swapped pair tile (MOE_B200_GEMM_SWAP=0 keeps the row-padded
+// one): bf16 operands, rows of one arrival group.
+bool use_swapped_pair() {
+    const char* env = getenv("MOE_B200_GEMM_SWAP");
+    return !(env && env[0] == '0');
 }
 
 template <typename Kernel>
@@ -1353,6 +1710,18 @@ cudaError_t launch_grouped_gemm(const void* a, const void* b, const int32_t* off
     if (tile == Tile::kPair) {
         const int64_t max_tiles =
             ((rows + kPairBM - 1) / kPairBM + experts) * static_cast<int64_t>(p.n_tiles);
+        if (!fp8 && groups == 1 && use_swapped_pair()) {
+            // SwiGLU loads each CTA's gate and up weight rows as two 64-row boxes
+            CUtensorMap map_w;
+            if (swiglu && !make_tensor_map(&map_w, b, static_cast<uint64_t>(b_rows * experts),
+                                           static_cast<uint64_t>(k_dim), false, kBoxRows / 2)) {
+                *error = "cuTensorMapEncodeTiled rejected an operand (pointer alignment or shape)";
+                return cudaErrorInvalidValue;
+            }
+            auto swapped = swiglu ? grouped_gemm_swap_kernel<true> : grouped_gemm_swap_kernel<false>;
+            return launch_pair(swapped, kSwapSmemBytes, info.swap_configured[swiglu], info.swap_clusters,
+                               info.sms, max_tiles, map_a, swiglu ? map_w : map_b, p, stream);
+        }
         auto pair = fp8 ? (swiglu ? grouped_gemm_pair_kernel<true, true> : grouped_gemm_pair_kernel<false, true>)
                         : (swiglu ? grouped_gemm_pair_kernel<true, false> : grouped_gemm_pair_kernel<false, false>);
         return launch_pair(pair, kPairSmemBytes, info.pair_configured[fp8][swiglu], info.pair_clusters,

@@ -25,14 +25,22 @@ pytestmark = [
 SENTINEL = -12345.0
 
 
-TILES = ["single", "pair"]
+TILES = ["single", "pair", "pair-padded"]
+
+
+def use_tile(monkeypatch, kind):
+    """single: the 128x256 one-CTA tile; pair: the CTA-pair tile with the
+    weights as the 256-row side and each expert's rows spread evenly over
+    tiles of N <= 256; pair-padded: the CTA-pair tile over 256-row blocks of
+    packed rows (what fp8 and arrival groups use)."""
+    monkeypatch.setenv("MOE_B200_GEMM_TILE", "single" if kind == "single" else "pair")
+    monkeypatch.setenv("MOE_B200_GEMM_SWAP", "0" if kind == "pair-padded" else "1")
 
 
 @pytest.fixture(autouse=True, params=TILES)
 def tile(request, monkeypatch):
-    """Run every test with each tile kind: the 128x256 one-CTA tile and the
-    256x256 CTA-pair tile."""
-    monkeypatch.setenv("MOE_B200_GEMM_TILE", request.param)
+    """Run every test with each tile kind."""
+    use_tile(monkeypatch, request.param)
     return request.param
 
 
@@ -172,7 +180,7 @@ def test_tile_kinds_give_identical_bits(ext, tile, monkeypatch, swiglu):
     a, w, offsets = make_problem([300, 0, 17, 129, 640, 5, 257], 448, 2 * 192, seed=11)
     results = {}
     for kind in TILES:
-        monkeypatch.setenv("MOE_B200_GEMM_TILE", kind)
+        use_tile(monkeypatch, kind)
         results[kind] = run_swiglu(ext, a, w, offsets) if swiglu else run_plain(ext, a, w, offsets)
     used = int(offsets[-1])
     for kind in TILES[1:]:
