@@ -182,7 +182,10 @@ int moe_grouped_gemm_e4m3(const void* a_q, const float* a_scale, const void* wei
  * `experts` experts (no counterpart in the reference): 1 = the 256-row
  * CTA-pair tile (cta_group::2), 0 = the 128-row one-CTA tile.  Every tile
  * kind gives the same bits; the choice only changes speed.  The environment
- * variable MOE_B200_GEMM_TILE=pair|single overrides it. */
+ * variable MOE_B200_GEMM_TILE=pair|single overrides it.  A bf16 pair launch
+ * runs the operand-swapped pair tile (weights as the 256-row side, each
+ * expert's rows spread over tiles of up to 256); MOE_B200_GEMM_SWAP=0 keeps
+ * the pair tile over 256-row blocks of packed rows. */
 int32_t moe_grouped_gemm_tile(int64_t rows, int32_t experts);
 
 /* ------------------------------------------------------- expert parallel */
