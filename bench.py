@@ -471,9 +471,17 @@ def algorithmic(workload, tokens):
                    gemm2_flops=2.0 * n * i * h)
 
 
-def gemm_kernel_name(block, rows, experts, swiglu=True):
+def gemm_kernel_name(block, rows, experts, swiglu=True, arrival_groups=False):
+    """The grouped GEMM kernel a launch of this shape runs, and its tile: a
+    bf16 pair launch of one arrival group runs the operand-swapped pair tile
+    unless MOE_B200_GEMM_SWAP=0."""
     tile = block.extension.grouped_gemm_tile(rows, experts)
-    base = "grouped_gemm_pair_kernel" if tile.startswith("pair") else "grouped_gemm_kernel"
+    if tile.startswith("pair"):
+        swapped = not arrival_groups and os.environ.get("MOE_B200_GEMM_SWAP", "1") != "0"
+        base = "grouped_gemm_swap_kernel" if swapped else "grouped_gemm_pair_kernel"
+        tile = "operand-swapped pair" if swapped else "pair"
+    else:
+        base = "grouped_gemm_kernel"
     return f"{base}<{1 if swiglu else 0}>", tile
 def stage_summary(workload, tokens, stage, block, rows, tf_peak, hbm_peak):
     """Per-stage ms, both GEMMs against the tensor peak, router and
@@ -830,7 +838,9 @@ def run_expert_parallel(args, rank, world, local):
     gemm1_flops = 2.0 * m["rows"] * h * 2 * i
     achieved = gemm1_flops / (stage["gemm1"] / 1e3) / 1e12
     capacity = block.exchange.grouped.shape[0] if block.backend == "p2p" else m["rows"]
-    gemm1_kernel, tile = gemm_kernel_name(block, capacity, workload.experts // world)
+    # the overlapped exchange feeds gate/up through arrival groups
+    gemm1_kernel, tile = gemm_kernel_name(block, capacity, workload.experts // world,
+                                          arrival_groups=getattr(block, "overlap", False) and world > 1)
     ms_per_step = m["ms_per_step"]
     graphed = m["graphed"]
     launches = ep_kernels_per_step(block, workload)

@@ -43,6 +43,7 @@ def test_reference_arm_prints_one_contract_line():
 def test_kernel_count_and_committed_traffic():
     assert bench.kernels_per_step(8) == 6 and bench.kernels_per_step(256) == 7
     assert bench.profiled_traffic("grouped_gemm_pair_kernel<1>") > 1.9e9
+    assert bench.profiled_traffic("grouped_gemm_swap_kernel<1>") > 1.9e9
     assert bench.profiled_traffic("no_such_kernel") is None
     hbm, tf, sustained, kind = bench.measured_peaks()
     assert hbm > 1000 and tf > 100 and kind in ("measured", "fallback")
