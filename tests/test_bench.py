@@ -40,6 +40,32 @@ def test_reference_arm_prints_one_contract_line():
     assert d["config"]["workload"] == bench.workload_config(WORKLOADS["mixtral"], 1)["workload"]
 
 
+def test_gemm_kernel_name_follows_the_launcher(monkeypatch):
+    """The roofline names the kernel the launcher runs: the operand-swapped
+    pair tile for bf16 pair launches of one arrival group, unless switched off."""
+
+    class Extension:
+        def __init__(self, tile):
+            self.tile = tile
+
+        def grouped_gemm_tile(self, rows, experts):
+            return self.tile
+
+    class Block:
+        def __init__(self, tile):
+            self.extension = Extension(tile)
+
+    monkeypatch.delenv("MOE_B200_GEMM_SWAP", raising=False)
+    assert bench.gemm_kernel_name(Block("pair"), 8256, 8) == ("grouped_gemm_swap_kernel<1>",
+                                                               "operand-swapped pair")
+    assert bench.gemm_kernel_name(Block("pair"), 8256, 8, arrival_groups=True) == (
+        "grouped_gemm_pair_kernel<1>", "pair")
+    assert bench.gemm_kernel_name(Block("single"), 1000, 8, swiglu=False) == (
+        "grouped_gemm_kernel<0>", "single")
+    monkeypatch.setenv("MOE_B200_GEMM_SWAP", "0")
+    assert bench.gemm_kernel_name(Block("pair"), 8256, 8)[0] == "grouped_gemm_pair_kernel<1>"
+
+
 def test_kernel_count_and_committed_traffic():
     assert bench.kernels_per_step(8) == 6 and bench.kernels_per_step(256) == 7
     assert bench.profiled_traffic("grouped_gemm_pair_kernel<1>") > 1.9e9
