@@ -117,6 +117,34 @@ def test_dispatch_is_deterministic_and_reusable(ext):
         assert torch.equal(ws.packed[: int(first[2][-1])], first[1][: int(first[2][-1])])
 
 
+@pytest.mark.parametrize("tokens,experts,topk", [(1, 8, 2), (3000, 8, 2), (4096, 8, 2),
+                                                 (2000, 64, 4), (5000, 8, 2)])
+def test_index_cluster_and_ticket_forms_agree(ext, monkeypatch, tokens, experts, topk):
+    """Up to 8 index chunks (8192 assignments) the index CTAs hand their chunk
+    totals to CTA 0 inside one thread-block cluster; MOE_B200_INDEX_CLUSTER=0
+    keeps the completion-ticket form.  Both give the same bits, out-of-range
+    counts included (3000 x 2: 6 chunks in a cluster of 8; 5000 x 2: 10
+    chunks, the ticket form either way)."""
+    x, ids, _ = transport_case(tokens, 64, experts, topk, torch.bfloat16, "zipf", seed=21)
+    ids = ids.clone()
+    ids[0, 0] = experts
+    ids[tokens // 2, topk - 1] = -1
+    results = {}
+    for form in ("1", "0"):
+        monkeypatch.setenv("MOE_B200_INDEX_CLUSTER", form)
+        ws = CudaWorkspace(tokens, 64, experts, topk, torch.bfloat16, alignment=8, extension=ext)
+        ws.dispatch(x.cuda(), ids.cuda())
+        used = int(ws.offsets[-1])
+        results[form] = (ws.counts.cpu(), ws.offsets.cpu(), ws.slots.cpu(), ws.inverse.cpu(),
+                         ws.packed[:used].cpu(), ws.invalid_ids())
+    for a, b in zip(results["1"], results["0"]):
+        if isinstance(a, torch.Tensor):
+            assert torch.equal(a, b)
+        else:
+            assert a == b
+    assert results["1"][-1] == 2
+
+
 def test_out_of_range_ids_are_skipped(ext):
     x = torch.randn(4, 16, dtype=torch.float16)
     ids = torch.tensor([[0, 9], [1, -1], [7, 2], [3, 3]], dtype=torch.int32)
